@@ -1,0 +1,552 @@
+"""Benchmark of the B200 FP16 matmul path on the 96-shape grid (and the other configurations).
+
+Default workload ``grid`` (the configuration the headline metric is quoted on): 8 (K, N)
+projection pairs of Llama-3-8B and Qwen2.5-7B x 12 values of M, FP16 operands N(0, 1)/sqrt(K)
+from seeded generators. Flow, as the reference's protocol (bank 1 selects, bank 2 scores):
+
+1. tuning (untimed): the Thompson-sampling bandit probes ``--budget`` candidates per shape
+   with live timed launches (every probe's output is checked against an FP32 reference);
+2. ``--warmup`` untimed passes, then ``--steps`` timed passes over the 96 shapes with each
+   shape's recommended variant through the public API (``action_expansion.launch``: output and
+   workspace allocated per call). Before every launch a 256 MiB write flushes L2; each launch is
+   bracketed by CUDA events on the launching stream. The same passes with cuBLAS
+   ``torch.matmul`` give the comparison;
+3. an end-to-end pass: host->device copies of A and B from pinned memory, the launch, and the
+   device->host copy of C, inside the events;
+4. on rank 0 at N=1, the CPU baseline: the oracle's FP32 BLAS product on a bounded sample.
+
+``value`` is the grid's aggregate TFLOP/s (total FLOPs of one pass / sum of per-shape median
+latencies), ``geomean_latency_vs_cublas`` the headline ratio. Under torchrun every rank runs the
+whole grid (replicas): value = sum over ranks' FLOPs / max over ranks' time.
+
+``--impl reference`` times the reference's CPU path (the oracle port) on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+METRIC = "geomean latency/cuBLAS torch.matmul, 96-shape FP16 grid; TFLOP/s & % roofline"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def _peaks() -> tuple[dict[str, float], str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {k: float(data[k]) for k in FALLBACK_PEAKS if k in data}, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def _workloads(name: str, shapes: str | None):
+    from heliostune_b200.configs import (
+        COLUMN_PARALLEL_WORKLOAD,
+        DECODE_WORKLOAD,
+        GRID_WORKLOADS,
+        SWEEP_WORKLOADS,
+        Workload,
+    )
+
+    if shapes:
+        out = []
+        for spec in shapes.split(","):
+            m, n, k = (int(v) for v in spec.lower().split("x"))
+            out.append(Workload(m=m, n=n, k=k, model="custom", projection="custom", regime=f"m{m}"))
+        return tuple(out)
+    return {
+        "grid": GRID_WORKLOADS,
+        "sweep": SWEEP_WORKLOADS,
+        "decode": (DECODE_WORKLOAD,),
+        "colpar": (COLUMN_PARALLEL_WORKLOAD,),
+    }[name]
+
+
+# ----------------------------------------------------------------------------------------------
+# Clock sampling during the timed region
+# ----------------------------------------------------------------------------------------------
+
+
+class ClockSampler:
+    QUERY = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, device: int) -> None:
+        self.device = device
+        self.proc: subprocess.Popen[str] | None = None
+
+    def __enter__(self) -> ClockSampler:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL,
+                text=True,
+            )
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        self.output = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.output, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.output, _ = self.proc.communicate()
+
+    def summary(self) -> dict[str, object]:
+        clocks, max_clock, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in getattr(self, "output", "").splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                clocks.append(float(parts[1]))
+                max_clock = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9], strict=True):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(clocks) if clocks else None,
+            "sm_max_mhz": max_clock,
+            "reasons": sorted(reasons),
+            "samples": len(clocks),
+        }
+
+
+# ----------------------------------------------------------------------------------------------
+# Our arm
+# ----------------------------------------------------------------------------------------------
+
+
+def _make_operands(workloads, device, seed_base: int):
+    """A per (K, M) and B per (K, N), shared across the shapes that use them."""
+    import torch
+
+    a_cache: dict[tuple[int, int], torch.Tensor] = {}
+    b_cache: dict[tuple[int, int], torch.Tensor] = {}
+    for w in workloads:
+        if (w.k, w.n) not in b_cache:
+            g = torch.Generator(device=device).manual_seed(seed_base + 7919 * w.k + w.n)
+            b_cache[(w.k, w.n)] = (torch.randn((w.k, w.n), generator=g, device=device) / math.sqrt(w.k)).to(torch.float16)
+        if (w.k, w.m) not in a_cache:
+            g = torch.Generator(device=device).manual_seed(seed_base + 104729 * w.k + w.m)
+            a_cache[(w.k, w.m)] = (torch.randn((w.m, w.k), generator=g, device=device) / math.sqrt(w.k)).to(torch.float16)
+    return {w.key: (a_cache[(w.k, w.m)], b_cache[(w.k, w.n)]) for w in workloads}
+
+
+def _launch_count(candidate, workload, sm_count: int) -> int:
+    from heliostune_b200.action_configs import SplitKConfig, StreamConfig, split_plan, stream_splits
+
+    config = candidate.config
+    if isinstance(config, SplitKConfig):
+        bk = 64 if config.block_k <= 64 else 128
+        return 1 + (split_plan(workload.k, bk, config.split_k)[1] > 1)
+    if isinstance(config, StreamConfig):
+        return 1 + (stream_splits(workload.m, workload.n, workload.k, config, sm_count) > 1)
+    return 1
+
+
+def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
+    import torch
+    import torch.distributed as dist
+
+    from heliostune_b200 import _native
+    from heliostune_b200.action_configs import b200_candidates_for
+    from heliostune_b200.action_expansion import fp32_reference, launch
+    from heliostune_b200.kernel import get_hardware_profile
+    from heliostune_b200.timing import do_bench, flush_buffer
+    from heliostune_b200.tuner import thompson_probe
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+    _native.library()  # fails loudly if the native path is missing
+    hardware = get_hardware_profile("B200", device)
+    sm_count = hardware.multiprocessor_count
+    workloads = _workloads(args.workload, args.shapes)
+    operands = _make_operands(workloads, device, seed_base=2)  # bank 2 tensors for scoring
+    tune_operands = _make_operands(workloads, device, seed_base=1)  # bank 1 tensors for tuning
+    flush = flush_buffer(device)
+
+    # ---- 1. tuning (bank 1) ------------------------------------------------------------
+    def measure(workload, candidate) -> float:
+        a, b = tune_operands[workload.key]
+        out = launch(a, b, candidate)
+        expected = fp32_reference(a, b)
+        scale = expected.abs().max().item()
+        err = (out.float() - expected).abs().max().item() / max(scale, 1e-30)
+        ok = bool(torch.all((out.float() - expected).abs() <= 1e-2 + 1e-2 * expected.abs()).item())
+        del expected, out
+        if not ok or not err <= 1e-2:
+            raise ValueError(f"parity failure (normwise {err:.3g})")
+        return do_bench(lambda: launch(a, b, candidate), warmup_ms=2.0, rep_ms=args.probe_ms, quantiles=(0.5,))[0]
+
+    t0 = time.perf_counter()
+    tuning = thompson_probe(workloads, b200_candidates_for, measure, hardware, budget=args.budget, policy_seed=args.seed)
+    tuning_s = time.perf_counter() - t0
+    chosen = {}
+    for w in workloads:
+        if w.key not in tuning.recommendations:
+            raise RuntimeError(f"no valid candidate for {w.key}")
+        chosen[w.key] = tuning.recommendations[w.key]
+    del tune_operands
+    torch.cuda.empty_cache()
+
+    # ---- 2. scored passes (bank 2) ---------------------------------------------------------
+    def one_pass(fn_for, events) -> None:
+        for i, w in enumerate(workloads):
+            a, b = operands[w.key]
+            fn = fn_for(w)
+            flush.zero_()
+            events[i][0].record()
+            fn(a, b)
+            events[i][1].record()
+
+    def ours_fn(w):
+        cand = chosen[w.key]
+        return lambda a, b: launch(a, b, cand)
+
+    def cublas_fn(w):
+        return lambda a, b: torch.matmul(a, b)
+
+    n = len(workloads)
+
+    def timed(fn_for, steps: int, warmup: int, sample_clocks: bool = False):
+        for _ in range(warmup):
+            one_pass(fn_for, [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)])
+        torch.cuda.synchronize()
+        events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)] for _ in range(steps)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        sampler = ClockSampler(local_rank) if sample_clocks else None
+        if sampler:
+            sampler.__enter__()
+        wall0 = time.perf_counter()
+        for s in range(steps):
+            one_pass(fn_for, events[s])
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - wall0
+        if sampler:
+            sampler.__exit__(None, None, None)
+        if world > 1:
+            dist.barrier()
+        per_shape = [[events[s][i][0].elapsed_time(events[s][i][1]) for s in range(steps)] for i in range(n)]
+        return per_shape, wall, (sampler.summary() if sampler else None)
+
+    ours_times, ours_wall, clocks = timed(ours_fn, args.steps, args.warmup, sample_clocks=True)
+    cublas_times, _, _ = timed(cublas_fn, args.steps, args.warmup)
+    ours_ms = [statistics.median(t) for t in ours_times]
+    cublas_ms = [statistics.median(t) for t in cublas_times]
+    total_flops = sum(w.flops for w in workloads)
+    pass_ms = sum(ours_ms)
+    ratios = [o / c for o, c in zip(ours_ms, cublas_ms, strict=True)]
+    geomean = math.exp(sum(math.log(r) for r in ratios) / len(ratios))
+
+    # ---- roofline of the dominant kernel family -------------------------------------------------
+    peaks, peak_source = _peaks()
+    fam_time: dict[str, float] = {}
+    fam_flops: dict[str, float] = {}
+    fam_bytes: dict[str, float] = {}
+    fam_launches: dict[str, int] = {}
+    for w, ms in zip(workloads, ours_ms, strict=True):
+        fam = chosen[w.key].family
+        fam_time[fam] = fam_time.get(fam, 0.0) + ms
+        fam_flops[fam] = fam_flops.get(fam, 0.0) + w.flops
+        fam_bytes[fam] = fam_bytes.get(fam, 0.0) + w.ideal_bytes
+        fam_launches[fam] = fam_launches.get(fam, 0) + 1
+    dominant = max(fam_time, key=fam_time.get)
+
+    def family_roofline(fam: str) -> dict[str, object]:
+        seconds = fam_time[fam] / 1e3
+        hbm_bound = fam in ("split_k", "stream")
+        if hbm_bound:
+            achieved = fam_bytes[fam] / seconds / 1e9
+            peak = peaks["hbm_gbs"]
+            unit = "GB/s"
+        else:
+            achieved = fam_flops[fam] / seconds / 1e12
+            peak = peaks["bf16_tflops"]
+            unit = "TFLOP/s"
+        return {
+            "bound": "hbm" if hbm_bound else "tensor",
+            "achieved": round(achieved, 2),
+            "peak": peak,
+            "unit": unit,
+            "frac": round(achieved / peak, 4),
+            "peak_source": f"{peak_source} (burst)",
+            "launches_per_pass": fam_launches[fam],
+            "share_of_pass": round(fam_time[fam] / pass_ms, 4),
+        }
+
+    roofline = family_roofline(dominant)
+    roofline["kernel"] = {"tile": "tile_gemm_kernel", "persistent": "tile_gemm_kernel (persistent grid)", "split_k": "stream_gemm_kernel + splitk_reduce_kernel", "stream": "stream_gemm_kernel"}[dominant]
+    roofline["traffic"] = _traffic_from_profiles(dominant)
+
+    # per-shape roofline fraction (slower of tensor and HBM bound)
+    shape_frac = []
+    for w, ms in zip(workloads, ours_ms, strict=True):
+        t_roof = max(w.flops / (peaks["bf16_tflops"] * 1e12), w.ideal_bytes / (peaks["hbm_gbs"] * 1e9))
+        shape_frac.append(t_roof / (ms / 1e3))
+
+    # ---- 3. end to end through the public API with host buffers ------------------------------
+    e2e_ms, h2d_bytes, d2h_bytes = _e2e_pass(workloads, operands, chosen, device, args.e2e_steps)
+
+    launches = sum(_launch_count(chosen[w.key], w, sm_count) for w in workloads) * args.steps
+
+    value = total_flops / (pass_ms / 1e3) / 1e12
+    e2e_value = total_flops / (sum(e2e_ms) / 1e3) / 1e12
+    if world > 1:
+        t = torch.tensor([pass_ms, sum(e2e_ms)], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        value = world * total_flops / (t[0].item() / 1e3) / 1e12
+        e2e_value = world * total_flops / (t[1].item() / 1e3) / 1e12
+
+    result: dict[str, object] = {
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(pass_ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16 (fp32 accumulate)",
+        "data": "synthetic: seeded N(0,1)/sqrt(K) FP16 operands",
+        "config": {
+            "workload": f"{args.workload}: {len(workloads)} shapes" if not args.shapes else f"shapes {args.shapes}",
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "l2": "256 MiB write before every launch",
+            "selection": f"Thompson bandit, {args.budget} probes per shape on bank-1 tensors; scored on bank-2 tensors",
+            "timing": "per-launch CUDA events on the launching stream; per-shape median over steps",
+        },
+        "geomean_latency_vs_cublas": round(geomean, 4),
+        "cublas_tflops": round(total_flops / (sum(cublas_ms) / 1e3) / 1e12, 3),
+        "shapes_faster_than_cublas": sum(r < 1.0 for r in ratios),
+        "geomean_roofline_frac": round(math.exp(sum(math.log(f) for f in shape_frac) / len(shape_frac)), 4),
+        "roofline": roofline,
+        "roofline_by_family": {f: family_roofline(f) for f in fam_time},
+        "e2e": {
+            "value": round(e2e_value, 3),
+            "unit": "TFLOP/s",
+            "h2d_bytes_per_step": h2d_bytes,
+            "d2h_bytes_per_step": d2h_bytes,
+            "note": "H2D of A and B from pinned memory + launch + D2H of C per shape, one pass",
+        },
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "wall_s_timed_region": round(ours_wall, 3),
+        "tuning_s": round(tuning_s, 1),
+        "status_bits": _native.status(local_rank),
+    }
+    if args.detail:
+        detail = ROOT / "gpurun_out" / f"bench_detail_{args.workload}.json"
+        detail.parent.mkdir(exist_ok=True)
+        detail.write_text(
+            json.dumps(
+                {
+                    "shapes": [
+                        {
+                            "workload": w.key,
+                            "m": w.m, "n": w.n, "k": w.k,
+                            "choice": chosen[w.key].key,
+                            "ours_ms": o,
+                            "cublas_ms": c,
+                            "ratio": o / c,
+                            "roofline_frac": f,
+                            "tflops": w.flops / (o / 1e3) / 1e12,
+                        }
+                        for w, o, c, f in zip(workloads, ours_ms, cublas_ms, shape_frac, strict=True)
+                    ],
+                    "tuning": tuning.to_dict(),
+                },
+                indent=1,
+            )
+        )
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(workloads, args.cpu_rows, args.cpu_budget_s)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result if rank == 0 else None
+
+
+def _traffic_from_profiles(family: str) -> float | None:
+    path = ROOT / "profiles" / "traffic.json"
+    if not path.exists():
+        return None
+    data = json.loads(path.read_text())
+    entry = data.get(family)
+    return None if entry is None else entry.get("bytes_per_launch")
+
+
+def _e2e_pass(workloads, operands, chosen, device, steps: int):
+    import torch
+
+    from heliostune_b200.action_expansion import launch
+
+    hosts = {}
+    for w in workloads:
+        a, b = operands[w.key]
+        hosts[w.key] = (
+            a.cpu().pin_memory(),
+            b.cpu().pin_memory(),
+            torch.empty((w.m, w.n), dtype=torch.float16).pin_memory(),
+        )
+    totals = [0.0] * len(workloads)
+    h2d = d2h = 0
+    for _ in range(steps + 1):  # first pass warms up
+        times = []
+        for i, w in enumerate(workloads):
+            a_h, b_h, c_h = hosts[w.key]
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            a = a_h.to(device, non_blocking=True)
+            b = b_h.to(device, non_blocking=True)
+            c = launch(a, b, chosen[w.key])
+            c_h.copy_(c, non_blocking=True)
+            end.record()
+            times.append((start, end))
+        torch.cuda.synchronize()
+        if _ > 0:
+            for i, (s, e) in enumerate(times):
+                totals[i] += s.elapsed_time(e) / steps
+    for w in workloads:
+        h2d += 2 * (w.m * w.k + w.k * w.n)
+        d2h += 2 * w.m * w.n
+    return totals, h2d, d2h
+
+
+# ----------------------------------------------------------------------------------------------
+# CPU baseline / reference arm
+# ----------------------------------------------------------------------------------------------
+
+
+def cpu_baseline(workloads, max_rows: int, budget_s: float) -> dict[str, object]:
+    """The oracle's FP32 BLAS product on the host cores, on a bounded sample of each shape.
+
+    Sample: the first ``min(M, max_rows)`` rows of A against the full B, inputs upcast from FP16
+    inside the timing; shapes are visited in grid order until ``budget_s`` of CPU time is spent.
+    """
+    from oracle import oracle
+
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    flops = 0.0
+    seconds = 0.0
+    sampled = 0
+    b_cache: dict[tuple[int, int], np.ndarray] = {}
+    for w in workloads:
+        rows = min(w.m, max_rows)
+        if (w.k, w.n) not in b_cache:
+            b_cache.clear()
+            b_cache[(w.k, w.n)] = (rng.standard_normal((w.k, w.n), dtype=np.float32) / math.sqrt(w.k)).astype(np.float16)
+        b = b_cache[(w.k, w.n)]
+        a = (rng.standard_normal((rows, w.k), dtype=np.float32) / math.sqrt(w.k)).astype(np.float16)
+        t0 = time.perf_counter()
+        oracle.gemm_fp32_blas(a, b)
+        seconds += time.perf_counter() - t0
+        flops += 2.0 * rows * w.n * w.k
+        sampled += 1
+        if seconds > budget_s:
+            break
+    return {
+        "value": round(flops / seconds / 1e12, 4),
+        "unit": "TFLOP/s",
+        "cores": cores,
+        "kind": "port",
+        "sample": f"{sampled} shapes, first min(M, {max_rows}) rows each, FP16 upcast + FP32 BLAS (numpy) on {cores} host threads",
+    }
+
+
+def run_reference(args: argparse.Namespace) -> dict[str, object] | None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    workloads = _workloads(args.workload, args.shapes)
+    samples = []
+    for _ in range(args.warmup):
+        cpu_baseline(workloads, args.cpu_rows, args.cpu_budget_s / 4)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        samples.append(cpu_baseline(workloads, args.cpu_rows, args.cpu_budget_s))
+    wall = time.perf_counter() - t0
+    value = statistics.median(s["value"] for s in samples)
+    base = samples[0]
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(wall / max(args.steps, 1) * 1e3, 1),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16 inputs, fp32 accumulate (CPU)",
+        "data": "synthetic: seeded N(0,1)/sqrt(K) FP16 operands",
+        "config": {"workload": f"{args.workload}: {len(workloads)} shapes", "parallelism": "host CPU"},
+        "cpu_baseline": {**base, "value": value},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=5)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--workload", choices=("grid", "sweep", "decode", "colpar"), default="grid")
+    parser.add_argument("--shapes", default=None, help="comma list of MxNxK overriding the workload")
+    parser.add_argument("--budget", type=int, default=8, help="bandit probes per shape")
+    parser.add_argument("--probe-ms", type=float, default=10.0)
+    parser.add_argument("--seed", type=int, default=0)
+    parser.add_argument("--e2e-steps", type=int, default=1)
+    parser.add_argument("--cpu-rows", type=int, default=64)
+    parser.add_argument("--cpu-budget-s", type=float, default=20.0)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--detail", action="store_true", help="write per-shape results under gpurun_out/")
+    args = parser.parse_args()
+    if args.warmup < 3 and args.impl == "ours" and not args.shapes:
+        print("note: fewer than 3 warm-up passes", file=sys.stderr)
+    result = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if result is not None:
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,270 @@
+"""The frozen action-expansion candidates plus the B200 weight-streaming family.
+
+``SplitKConfig``, ``ActionCandidate``, the frozen candidate tuples, ``candidates_for`` and
+``action_set_manifest`` keep the reference's names, keys and membership
+(``src/heliostune/action_configs.py:17-131``). Enumeration imports neither torch nor the native
+library, as in the reference.
+
+:class:`StreamConfig` is new: a swap-AB tcgen05 weight-streaming GEMM for ``M <= 256`` whose
+split factor can be chosen per shape so the grid fills the 148 SMs. It is offered to the bandit
+next to the frozen candidates by :func:`b200_candidates_for`.
+"""
+
+from __future__ import annotations
+
+from dataclasses import asdict, dataclass
+from typing import Any, Literal
+
+from heliostune_b200.configs import DEFAULT_CONFIGS, HopperGemmConfig, KernelConfig, Workload
+from heliostune_b200.errors import SchemaError
+from heliostune_b200.validation import exact_int
+
+#: Largest M the reference's split-K launcher accepts (``action_configs.py:17``).
+SPLIT_K_M_LIMIT = 31
+
+#: Largest M the B200 weight-streaming kernel accepts (the UMMA N of its swapped MMA).
+STREAM_M_LIMIT = 256
+
+
+def _power_of_two(value: int) -> bool:
+    return value > 0 and value & (value - 1) == 0
+
+
+@dataclass(frozen=True, slots=True)
+class SplitKConfig:
+    """Split-K GEMM for ``1 <= M <= 31``: FP32 partials, then a fixed-order reduction.
+
+    On a B200 (swap-AB tcgen05): ``block_n`` is the UMMA M, i.e. the columns of C one CTA owns
+    (64 or 128); ``block_m`` is the granularity the rows of A are padded to for the UMMA N (all
+    ``M <= 31`` rows are held by one CTA); ``block_k`` is the K extent of one shared-memory stage;
+    ``num_stages`` is the depth of the TMA ring; ``split_k`` is the number of contiguous
+    ``block_k``-aligned K intervals, each written to its own FP32 partial and summed in split
+    order by a second kernel. ``num_warps`` is kept for the key.
+    """
+
+    block_m: int
+    block_n: int
+    block_k: int
+    num_warps: int
+    num_stages: int
+    split_k: int
+
+    def __post_init__(self) -> None:
+        for name in ("block_m", "block_n", "block_k", "num_warps", "num_stages", "split_k"):
+            exact_int(getattr(self, name), context=f"split-K config {name}", minimum=1)
+        for name in ("block_m", "block_n", "block_k", "split_k"):
+            if not _power_of_two(getattr(self, name)):
+                raise SchemaError(f"{name} must be a power of two")
+        for name in ("block_m", "block_n", "block_k"):
+            if getattr(self, name) < 16:
+                raise SchemaError(f"{name} must be at least 16")
+        if self.num_warps not in (1, 2, 4, 8):
+            raise SchemaError("num_warps must be one of 1, 2, 4, or 8")
+        if self.split_k < 2:
+            raise SchemaError("split_k must be at least 2")
+
+    @property
+    def key(self) -> str:
+        return (
+            f"m{self.block_m}n{self.block_n}k{self.block_k}"
+            f"-w{self.num_warps}s{self.num_stages}-split{self.split_k}"
+        )
+
+    def to_dict(self) -> dict[str, int]:
+        return asdict(self)
+
+
+@dataclass(frozen=True, slots=True)
+class StreamConfig:
+    """B200 weight-streaming GEMM for ``1 <= M <= 256`` (no reference counterpart).
+
+    The CTA owns ``block_n`` (=128, the UMMA M) columns of C and all M rows (padded to a multiple
+    of 16 for the UMMA N). ``block_k`` and ``num_stages`` shape the TMA ring. ``split_k`` = 0 asks
+    the launcher to choose the split so that ``ceil(N/128) * split`` CTAs fill the SMs; a positive
+    value is used as given. One split writes C directly; more write FP32 partials that a second
+    kernel sums in split order.
+    """
+
+    block_m: int
+    block_n: int
+    block_k: int
+    num_warps: int
+    num_stages: int
+    split_k: int = 0
+
+    def __post_init__(self) -> None:
+        for name in ("block_m", "block_n", "block_k", "num_warps", "num_stages"):
+            exact_int(getattr(self, name), context=f"stream config {name}", minimum=1)
+        exact_int(self.split_k, context="stream config split_k", minimum=0)
+        for name in ("block_m", "block_n", "block_k"):
+            if not _power_of_two(getattr(self, name)):
+                raise SchemaError(f"{name} must be a power of two")
+        if not 16 <= self.block_m <= STREAM_M_LIMIT:
+            raise SchemaError(f"block_m must be between 16 and {STREAM_M_LIMIT}")
+        if self.block_n != 128:
+            raise SchemaError("block_n must be 128 (the UMMA M of the swapped MMA)")
+        if self.block_k not in (64, 128):
+            raise SchemaError("block_k must be 64 or 128")
+        if self.num_warps not in (1, 2, 4, 8):
+            raise SchemaError("num_warps must be one of 1, 2, 4, or 8")
+
+    @property
+    def key(self) -> str:
+        split = "auto" if self.split_k == 0 else str(self.split_k)
+        return (
+            f"stream-m{self.block_m}n{self.block_n}k{self.block_k}"
+            f"-w{self.num_warps}s{self.num_stages}-split{split}"
+        )
+
+    def to_dict(self) -> dict[str, int]:
+        return asdict(self)
+
+
+ActionConfig = KernelConfig | HopperGemmConfig | SplitKConfig | StreamConfig
+
+
+@dataclass(frozen=True, slots=True)
+class ActionCandidate:
+    """An immutable launch configuration with a family-qualified identity."""
+
+    config: ActionConfig
+
+    def __post_init__(self) -> None:
+        if not isinstance(self.config, KernelConfig | HopperGemmConfig | SplitKConfig | StreamConfig):
+            raise TypeError("candidate config must be a tile, persistent, split-K or stream config")
+
+    @property
+    def family(self) -> Literal["tile", "persistent", "split_k", "stream"]:
+        if isinstance(self.config, KernelConfig):
+            return "tile"
+        if isinstance(self.config, HopperGemmConfig):
+            return "persistent"
+        if isinstance(self.config, SplitKConfig):
+            return "split_k"
+        return "stream"
+
+    @property
+    def key(self) -> str:
+        return f"{self.family}:{self.config.key}"
+
+    def to_dict(self) -> dict[str, int | bool]:
+        return dict(self.config.to_dict())
+
+
+def _sorted(candidates: tuple[ActionCandidate, ...]) -> tuple[ActionCandidate, ...]:
+    return tuple(sorted(candidates, key=lambda c: c.key))
+
+
+#: The six ordinary/persistent candidates (``action_configs.py:88-101``).
+NON_SPLIT_CANDIDATES: tuple[ActionCandidate, ...] = _sorted(
+    (
+        ActionCandidate(KernelConfig(128, 128, 64, 4, 5)),
+        ActionCandidate(KernelConfig(128, 256, 64, 8, 4)),
+        ActionCandidate(KernelConfig(256, 128, 64, 8, 4)),
+        ActionCandidate(KernelConfig(128, 128, 128, 8, 3)),
+        ActionCandidate(HopperGemmConfig(128, 128, 64, 4, 4)),
+        ActionCandidate(HopperGemmConfig(128, 256, 64, 8, 3)),
+    )
+)
+#: The four split-K candidates for ``M <= 31`` (``action_configs.py:102-111``).
+SPLIT_K_CANDIDATES: tuple[ActionCandidate, ...] = _sorted(
+    (
+        ActionCandidate(SplitKConfig(16, 64, 64, 4, 3, 4)),
+        ActionCandidate(SplitKConfig(16, 64, 64, 4, 3, 16)),
+        ActionCandidate(SplitKConfig(16, 128, 64, 4, 3, 4)),
+        ActionCandidate(SplitKConfig(16, 128, 64, 4, 3, 16)),
+    )
+)
+ALL_CANDIDATES: tuple[ActionCandidate, ...] = _sorted((*NON_SPLIT_CANDIDATES, *SPLIT_K_CANDIDATES))
+
+
+def candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:
+    """The reference's frozen candidates for a workload; no measurement influences them."""
+    return ALL_CANDIDATES if workload.m <= SPLIT_K_M_LIMIT else NON_SPLIT_CANDIDATES
+
+
+def stream_block_m(m: int) -> int:
+    """Padded row count of the weight-streaming kernel: the next multiple of 16 as power of 2."""
+    block = 16
+    while block < m:
+        block *= 2
+    return block
+
+
+def stream_candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:
+    """B200 weight-streaming candidates for ``M <= 256`` (empty above)."""
+    if workload.m > STREAM_M_LIMIT:
+        return ()
+    bm = stream_block_m(workload.m)
+    return _sorted(
+        (
+            ActionCandidate(StreamConfig(bm, 128, 64, 4, 8, 0)),
+            ActionCandidate(StreamConfig(bm, 128, 128, 4, 4, 0)),
+            ActionCandidate(StreamConfig(bm, 128, 64, 4, 4, 0)),
+        )
+    )
+
+
+def b200_candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:
+    """Everything the B200 tuner may probe: the frozen set plus the streaming family."""
+    return _sorted((*candidates_for(workload), *stream_candidates_for(workload)))
+
+
+def action_set_manifest() -> dict[str, list[dict[str, Any]]]:
+    """The frozen old/new action identities (``action_configs.py:122-131``)."""
+    return {
+        "old": [
+            {"family": "old", "config_key": c.key, "config": c.to_dict()} for c in DEFAULT_CONFIGS
+        ],
+        "new": [
+            {"family": c.family, "config_key": c.key, "config": c.to_dict()} for c in ALL_CANDIDATES
+        ],
+    }
+
+
+# --------------------------------------------------------------------------------------------
+# Launch planning of the weight-streaming kernels, shared by the launcher and the features.
+# --------------------------------------------------------------------------------------------
+
+#: Shared memory of one B200 SM and the per-CTA share the runtime reserves.
+SMEM_PER_SM = 233472
+SMEM_RESERVED_PER_CTA = 1024
+#: Bytes of barriers, the TMEM address slot and alignment slack in a streaming CTA.
+STREAM_SMEM_OVERHEAD = 2048
+
+
+def stream_smem_bytes(block_m: int, block_n: int, block_k: int, stages: int) -> int:
+    """Dynamic shared memory of one streaming CTA: the ring of B^T and A^T tiles."""
+    return stages * (block_n + block_m) * block_k * 2 + STREAM_SMEM_OVERHEAD
+
+
+def stream_ctas_per_sm(block_m: int, block_n: int, block_k: int, stages: int) -> int:
+    per_cta = stream_smem_bytes(block_m, block_n, block_k, stages) + SMEM_RESERVED_PER_CTA
+    by_smem = SMEM_PER_SM // per_cta
+    tmem_columns = max(32, block_m)
+    by_tmem = 512 // tmem_columns
+    return max(1, min(by_smem, by_tmem, 4))
+
+
+def split_plan(k: int, block_k: int, splits: int) -> tuple[int, int]:
+    """``(k_blocks_per_split, effective_splits)`` for contiguous block-aligned K intervals.
+
+    Restates the reference's interval rule (``action_expansion.py:79-80``):
+    ``tiles_per_split = cdiv(cdiv(K, BK), S)``. Splits that would start past K are dropped,
+    so every launched split owns at least one K block.
+    """
+    k_blocks = -(-k // block_k)
+    per_split = -(-k_blocks // splits)
+    return per_split, -(-k_blocks // per_split)
+
+
+def stream_splits(m: int, n: int, k: int, config: StreamConfig, sm_count: int) -> int:
+    """The split factor a :class:`StreamConfig` launches with on a GPU with ``sm_count`` SMs."""
+    if config.split_k:
+        return split_plan(k, config.block_k, config.split_k)[1]
+    n_tiles = -(-n // config.block_n)
+    slots = sm_count * stream_ctas_per_sm(
+        config.block_m, config.block_n, config.block_k, config.num_stages
+    )
+    wanted = max(1, slots // n_tiles)
+    return split_plan(k, config.block_k, wanted)[1]

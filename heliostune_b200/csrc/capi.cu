@@ -1,0 +1,757 @@
+// C ABI of heliostune_b200: argument checks, TMA tensor maps, workspace planning and the choice
+// of kernel instantiation for each configuration. See include/heliostune_b200.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "../../include/heliostune_b200.h"
+#include "gemm_stream.cuh"
+#include "gemm_tile.cuh"
+#include "rmsnorm.cuh"
+
+namespace hst {
+namespace {
+
+// ------------------------------------------------------------------------------------------
+// Errors
+// ------------------------------------------------------------------------------------------
+
+thread_local std::string t_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_error = buf;
+  return code;
+}
+
+#define HST_CUDA(call)                                                                   \
+  do {                                                                                   \
+    cudaError_t err_ = (call);                                                           \
+    if (err_ != cudaSuccess)                                                             \
+      return fail(HST_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(err_));       \
+  } while (0)
+
+#define HST_TRY(call)          \
+  do {                                \
+    int rc_ = (call);                 \
+    if (rc_ != HST_OK) return rc_;    \
+  } while (0)
+
+// ------------------------------------------------------------------------------------------
+// Per-device state
+// ------------------------------------------------------------------------------------------
+
+__device__ int g_status_word;  // OR of StatusBits raised by kernels on this device
+
+constexpr int kMaxDevices = 64;
+constexpr int kMaxDynamicSmem = 232448;  // 227 KB per CTA on sm_100
+constexpr int kSmemPerSm = 233472;       // 228 KB per SM
+constexpr int kSmemReservedPerCta = 1024;
+
+struct DeviceState {
+  std::atomic<bool> ready{false};
+  int sm_count = 0;
+  int* status = nullptr;
+};
+DeviceState g_devices[kMaxDevices];
+std::mutex g_device_mutex;
+
+int device_state(DeviceState** out) {
+  int dev = 0;
+  HST_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(HST_ERR_INVALID, "device %d out of range", dev);
+  DeviceState& s = g_devices[dev];
+  if (!s.ready.load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(g_device_mutex);
+    if (!s.ready.load(std::memory_order_relaxed)) {
+      HST_CUDA(cudaDeviceGetAttribute(&s.sm_count, cudaDevAttrMultiProcessorCount, dev));
+      HST_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&s.status), g_status_word));
+      s.ready.store(true, std::memory_order_release);
+    }
+  }
+  *out = &s;
+  return HST_OK;
+}
+
+// Raises the dynamic shared-memory limit of a kernel once per device.
+template <typename Kernel>
+int allow_smem(Kernel kernel, std::atomic<uint64_t>& done_mask) {
+  int dev = 0;
+  HST_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << dev;
+  if (!(done_mask.load(std::memory_order_acquire) & bit)) {
+    HST_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  kMaxDynamicSmem));
+    done_mask.fetch_or(bit, std::memory_order_release);
+  }
+  return HST_OK;
+}
+
+// Dynamic shared memory to request so that co-resident CTAs never ask for more than the SM's
+// 512 TMEM columns in total (tcgen05.alloc would otherwise stall a CTA until another exits).
+int smem_for_tmem(int smem, int tmem_cols) {
+  const int max_ctas = 512 / tmem_cols;
+  const int by_smem = kSmemPerSm / (smem + kSmemReservedPerCta);
+  if (by_smem <= max_ctas) return smem;
+  return kSmemPerSm / max_ctas - kSmemReservedPerCta + 1;
+}
+
+// ------------------------------------------------------------------------------------------
+// TMA tensor maps
+// ------------------------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+cudaError_t g_encode_error = cudaSuccess;
+
+int encode_tiled_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                    uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+  std::call_once(g_encode_once, [] {
+    cudaDriverEntryPointQueryResult q;
+    g_encode_error = cudaGetDriverEntryPointByVersion(
+        "cuTensorMapEncodeTiled", reinterpret_cast<void**>(&g_encode), 12000, cudaEnableDefault,
+        &q);
+    if (g_encode_error == cudaSuccess && q != cudaDriverEntryPointSuccess) {
+      g_encode_error = cudaErrorNotSupported;
+    }
+  });
+  if (g_encode == nullptr) {
+    return fail(HST_ERR_CUDA, "cuTensorMapEncodeTiled unavailable: %s",
+                cudaGetErrorString(g_encode_error));
+  }
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_stride_elems * 2};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t elem_strides[2] = {1, 1};
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base),
+                              dims, strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail(HST_ERR_CUDA,
+                "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu, row stride %llu, box %u x %u",
+                static_cast<int>(r), static_cast<unsigned long long>(inner),
+                static_cast<unsigned long long>(outer),
+                static_cast<unsigned long long>(row_stride_elems), box_inner, box_outer);
+  }
+  return HST_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Operand layouts
+// ------------------------------------------------------------------------------------------
+
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+int64_t round_up(int64_t a, int64_t b) { return cdiv(a, b) * b; }
+
+// A row-major view [rows, cols] with element strides (s0, s1).
+struct View {
+  const __half* ptr;
+  int64_t rows, cols, s0, s1;
+};
+
+// Whether a TMA tensor map can describe the view directly: unit inner stride, 16-byte aligned
+// base and row stride. Strides of size-1 dimensions do not matter.
+bool tma_compatible(const View& v) {
+  if (reinterpret_cast<uintptr_t>(v.ptr) & 15) return false;
+  if (v.cols > 1 && v.s1 != 1) return false;
+  if (v.rows > 1 && (v.s0 < v.cols || (v.s0 * 2) % 16 != 0)) return false;
+  return true;
+}
+
+// Row stride a tensor map is given for a TMA-compatible view.
+int64_t tma_row_stride(const View& v) { return v.rows > 1 ? v.s0 : round_up(v.cols, 8); }
+
+__global__ void pack_fp16_kernel(const __half* __restrict__ src, int64_t s0, int64_t s1,
+                                 int64_t rows, int64_t cols, __half* __restrict__ dst,
+                                 int64_t ld) {
+  const int64_t total = rows * ld;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / ld, c = i % ld;
+    dst[i] = c < cols ? src[r * s0 + c * s1] : __float2half_rn(0.f);
+  }
+}
+
+__global__ void copy_fp16_2d_kernel(const __half* __restrict__ src, int64_t lds, int64_t rows,
+                                    int64_t cols, __half* __restrict__ dst, int64_t ldd) {
+  const int64_t total = rows * cols;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cols, c = i % cols;
+    dst[r * ldd + c] = src[r * lds + c];
+  }
+}
+
+__global__ void fill_zero_fp16_kernel(__half* __restrict__ dst, int64_t ldd, int64_t rows,
+                                      int64_t cols) {
+  const int64_t total = rows * cols;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    dst[(i / cols) * ldd + i % cols] = __float2half_rn(0.f);
+  }
+}
+
+__global__ void probe_timeout_kernel(int* status, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // Nothing ever arrives on `bar`: the wait must run out and report.
+    if (!mbar_wait(&bar, 0, &abort_flag, limit_ns)) atomicOr(status, kStatusProbeTimeout);
+  }
+}
+
+int grid_for(int64_t total, int sms) {
+  const int64_t blocks = cdiv(total, 256);
+  return static_cast<int>(blocks < int64_t(sms) * 8 ? (blocks > 0 ? blocks : 1) : int64_t(sms) * 8);
+}
+
+// ------------------------------------------------------------------------------------------
+// Workspace plan
+// ------------------------------------------------------------------------------------------
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+struct Plan {
+  int family;
+  // tile / persistent
+  int um, ma, bn, bk, stages, group_m;
+  // split-K / stream
+  int nt, mp, splits, kb_per_split;
+  // workspace offsets (bytes) and sizes
+  bool pack_a, pack_b, c_tmp;
+  int64_t lda_p, ldb_p, ldc_p;
+  size_t off_a, off_b, off_c, off_p, total;
+};
+
+int split_plan(int64_t k, int bk, int requested, int* kb_per_split, int* splits) {
+  const int64_t k_blocks = cdiv(k, bk);
+  const int64_t per = cdiv(k_blocks, requested);
+  *kb_per_split = static_cast<int>(per);
+  *splits = static_cast<int>(cdiv(k_blocks, per));
+  return HST_OK;
+}
+
+int stream_ctas_per_sm(int mp, int nt, int bk, int stages) {
+  const int smem = stages * (nt + mp) * bk * 2 + 2048;
+  const int by_smem = kSmemPerSm / (smem + kSmemReservedPerCta);
+  const int by_tmem = 512 / (mp <= 32 ? 32 : mp);
+  int c = by_smem < by_tmem ? by_smem : by_tmem;
+  if (c > 4) c = 4;
+  return c < 1 ? 1 : c;
+}
+
+int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t m, int64_t n,
+              int64_t k, int sms, Plan* p) {
+  if (cfg == nullptr) return fail(HST_ERR_INVALID, "configuration is null");
+  *p = Plan{};
+  p->family = cfg->family;
+  const int bm = cfg->block_m, bn = cfg->block_n, bk = cfg->block_k;
+  auto pow2 = [](int v) { return v > 0 && (v & (v - 1)) == 0; };
+  if (!pow2(bm) || !pow2(bn) || !pow2(bk) || cfg->num_stages < 1 || cfg->num_warps < 1)
+    return fail(HST_ERR_INVALID, "block sizes must be powers of two and stages/warps positive");
+  switch (cfg->family) {
+    case HST_FAMILY_TILE:
+    case HST_FAMILY_PERSISTENT: {
+      if (cfg->group_m < 1) return fail(HST_ERR_INVALID, "group_m must be positive");
+      if (bm <= 64) {
+        p->um = 64;
+        p->ma = 1;
+      } else if (bm == 128) {
+        p->um = 128;
+        p->ma = 1;
+      } else if (bm == 256) {
+        p->um = 128;
+        p->ma = 2;
+      } else {
+        return fail(HST_ERR_UNSUPPORTED, "block_m %d has no B200 tile kernel (max 256)", bm);
+      }
+      p->bn = bn < 64 ? 64 : bn;
+      p->bk = bk < 64 ? 64 : bk;
+      if (p->bn > 256 || p->bk > 128 || (p->ma == 2 && p->bn > 128))
+        return fail(HST_ERR_UNSUPPORTED, "tile %dx%dx%d has no B200 kernel", bm, bn, bk);
+      p->stages = cfg->num_stages < 2 ? 2 : (cfg->num_stages > kMaxStages ? kMaxStages : cfg->num_stages);
+      p->group_m = cfg->group_m;
+      break;
+    }
+    case HST_FAMILY_SPLIT_K: {
+      if (m < 1 || m > 31 || n < 1 || k < 1)
+        return fail(HST_ERR_INVALID, "split-K requires 1 <= M <= 31 and positive N and K");
+      if (cfg->split_k < 2 || !pow2(cfg->split_k))
+        return fail(HST_ERR_INVALID, "split_k must be a power of two of at least 2");
+      if (bn != 64 && bn != 128)
+        return fail(HST_ERR_UNSUPPORTED, "split-K block_n %d has no B200 kernel (64 or 128)", bn);
+      p->nt = bn;
+      p->mp = m <= 16 ? 16 : 32;
+      p->bk = bk <= 64 ? 64 : 128;
+      p->stages = cfg->num_stages < 2 ? 2 : (cfg->num_stages > kStreamMaxStages ? kStreamMaxStages : cfg->num_stages);
+      split_plan(k, p->bk, cfg->split_k, &p->kb_per_split, &p->splits);
+      break;
+    }
+    case HST_FAMILY_STREAM: {
+      if (m < 1 || m > 256 || n < 1 || k < 1)
+        return fail(HST_ERR_INVALID, "the stream family requires 1 <= M <= 256 and positive N and K");
+      if (bm < 16 || bm > 256 || bm < m)
+        return fail(HST_ERR_INVALID, "stream block_m %d must cover M=%lld (16..256)", bm,
+                    static_cast<long long>(m));
+      if (bn != 128) return fail(HST_ERR_UNSUPPORTED, "stream block_n must be 128");
+      if (bk != 64 && bk != 128) return fail(HST_ERR_UNSUPPORTED, "stream block_k must be 64 or 128");
+      if (cfg->split_k < 0) return fail(HST_ERR_INVALID, "split_k must be >= 0");
+      p->nt = 128;
+      p->mp = bm;
+      p->bk = bk;
+      p->stages = cfg->num_stages < 2 ? 2 : (cfg->num_stages > kStreamMaxStages ? kStreamMaxStages : cfg->num_stages);
+      int requested = cfg->split_k;
+      if (requested == 0) {
+        const int64_t n_tiles = cdiv(n, 128);
+        const int64_t slots = int64_t(sms) * stream_ctas_per_sm(p->mp, p->nt, p->bk, p->stages);
+        const int64_t want = slots / n_tiles;
+        requested = static_cast<int>(want < 1 ? 1 : want);
+      }
+      split_plan(k, p->bk, requested, &p->kb_per_split, &p->splits);
+      break;
+    }
+    default:
+      return fail(HST_ERR_INVALID, "unknown family %d", cfg->family);
+  }
+
+  const bool is_stream = p->family == HST_FAMILY_SPLIT_K || p->family == HST_FAMILY_STREAM;
+  p->pack_a = !tma_compatible(a);
+  p->pack_b = !tma_compatible(b);
+  p->lda_p = round_up(k, 8);
+  p->ldb_p = round_up(n, 8);
+  p->c_tmp = !is_stream && (n % 8 != 0);
+  p->ldc_p = round_up(n, 8);
+  size_t off = 0;
+  p->off_a = off;
+  if (p->pack_a) off = align_up(off + size_t(m) * p->lda_p * 2);
+  p->off_b = off;
+  if (p->pack_b) off = align_up(off + size_t(k) * p->ldb_p * 2);
+  p->off_c = off;
+  if (p->c_tmp) off = align_up(off + size_t(m) * p->ldc_p * 2);
+  p->off_p = off;
+  if (is_stream && p->splits > 1) off = align_up(off + size_t(p->splits) * m * n * 4);
+  p->total = off;
+  return HST_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Tile / persistent launch
+// ------------------------------------------------------------------------------------------
+
+struct Operands {
+  const __half* a;
+  int64_t lda;  // row stride a tensor map can use
+  const __half* b;
+  int64_t ldb;
+  __half* c;
+  int64_t ldc;
+  int m, n, k;
+};
+
+template <int UM, int MA, int BN, int BK>
+int launch_tile(const DeviceState& dev, const Operands& o, int stages, int group_m,
+                bool persistent, cudaStream_t stream) {
+  using S = TileShape<UM, MA, BN, BK>;
+  static std::atomic<uint64_t> smem_done{0};
+  HST_TRY(allow_smem(tile_gemm_kernel<UM, MA, BN, BK>, smem_done));
+  while (stages > 2 && S::smem_bytes(stages) > kMaxDynamicSmem) --stages;
+  if (S::smem_bytes(stages) > kMaxDynamicSmem)
+    return fail(HST_ERR_UNSUPPORTED, "tile %dx%dx%d does not fit shared memory", UM * MA, BN, BK);
+  CUtensorMap ma_, mb_, mc_;
+  HST_TRY(encode_tiled_2d(&ma_, o.a, o.k, o.m, o.lda, 64, UM));
+  HST_TRY(encode_tiled_2d(&mb_, o.b, o.n, o.k, o.ldb, 64, BK));
+  HST_TRY(encode_tiled_2d(&mc_, o.c, o.n, o.m, o.ldc, 64, S::kRowsPerWarp));
+  TileArgs args;
+  args.m = o.m;
+  args.n = o.n;
+  args.k = o.k;
+  args.tiles_m = static_cast<int>(cdiv(o.m, UM * MA));
+  args.tiles_n = static_cast<int>(cdiv(o.n, BN));
+  args.num_tiles = args.tiles_m * args.tiles_n;
+  args.k_blocks = static_cast<int>(cdiv(o.k, BK));
+  args.group_m = group_m;
+  args.stages = stages;
+  args.status = dev.status;
+  const int smem = smem_for_tmem(S::smem_bytes(stages), S::kTmemCols);
+  const int per_sm = kSmemPerSm / (smem + kSmemReservedPerCta);
+  int grid = args.num_tiles;
+  if (persistent) {
+    const int slots = dev.sm_count * (per_sm > 0 ? per_sm : 1);
+    grid = grid < slots ? grid : slots;
+  }
+  tile_gemm_kernel<UM, MA, BN, BK><<<grid, kTileThreads, smem, stream>>>(ma_, mb_, mc_, args);
+  HST_CUDA(cudaGetLastError());
+  return HST_OK;
+}
+
+int dispatch_tile(const DeviceState& dev, const Plan& p, const Operands& o, bool persistent,
+                  cudaStream_t stream) {
+#define HST_TILE_CASE(UM_, MA_, BN_, BK_)                                          \
+  if (p.um == UM_ && p.ma == MA_ && p.bn == BN_ && p.bk == BK_)                    \
+    return launch_tile<UM_, MA_, BN_, BK_>(dev, o, p.stages, p.group_m, persistent, stream);
+  HST_TILE_CASE(64, 1, 64, 64)
+  HST_TILE_CASE(64, 1, 128, 64)
+  HST_TILE_CASE(64, 1, 256, 64)
+  HST_TILE_CASE(64, 1, 64, 128)
+  HST_TILE_CASE(64, 1, 128, 128)
+  HST_TILE_CASE(128, 1, 64, 64)
+  HST_TILE_CASE(128, 1, 128, 64)
+  HST_TILE_CASE(128, 1, 256, 64)
+  HST_TILE_CASE(128, 1, 64, 128)
+  HST_TILE_CASE(128, 1, 128, 128)
+  HST_TILE_CASE(128, 1, 256, 128)
+  HST_TILE_CASE(128, 2, 64, 64)
+  HST_TILE_CASE(128, 2, 128, 64)
+  HST_TILE_CASE(128, 2, 64, 128)
+  HST_TILE_CASE(128, 2, 128, 128)
+#undef HST_TILE_CASE
+  return fail(HST_ERR_UNSUPPORTED, "no tile kernel for UMMA M %d x %d atoms, N %d, K %d", p.um,
+              p.ma, p.bn, p.bk);
+}
+
+// ------------------------------------------------------------------------------------------
+// Split-K / stream launch
+// ------------------------------------------------------------------------------------------
+
+template <int NT, int MP, int BK>
+int launch_stream(const DeviceState& dev, const Operands& o, int stages, int splits,
+                  int kb_per_split, float* partials, cudaStream_t stream) {
+  using S = StreamShape<NT, MP, BK>;
+  static std::atomic<uint64_t> smem_done{0};
+  HST_TRY(allow_smem(stream_gemm_kernel<NT, MP, BK>, smem_done));
+  while (stages > 2 && S::smem_bytes(stages) > kMaxDynamicSmem) --stages;
+  if (S::smem_bytes(stages) > kMaxDynamicSmem)
+    return fail(HST_ERR_UNSUPPORTED, "stream tile does not fit shared memory");
+  CUtensorMap ma_, mb_;
+  HST_TRY(encode_tiled_2d(&ma_, o.a, o.k, o.m, o.lda, 64, MP));
+  HST_TRY(encode_tiled_2d(&mb_, o.b, o.n, o.k, o.ldb, 64, BK));
+  StreamArgs args;
+  args.m = o.m;
+  args.n = o.n;
+  args.k = o.k;
+  args.k_blocks = static_cast<int>(cdiv(o.k, BK));
+  args.kb_per_split = kb_per_split;
+  args.stages = stages;
+  args.status = dev.status;
+  args.partials = splits > 1 ? partials : nullptr;
+  args.c = o.c;
+  args.ldc = o.ldc;
+  const int smem = smem_for_tmem(S::smem_bytes(stages), S::kTmemCols);
+  const dim3 grid(static_cast<unsigned>(cdiv(o.n, NT)), static_cast<unsigned>(splits));
+  stream_gemm_kernel<NT, MP, BK><<<grid, kStreamThreads, smem, stream>>>(ma_, mb_, args);
+  HST_CUDA(cudaGetLastError());
+  if (splits > 1) {
+    const int64_t threads = int64_t(o.m) * cdiv(o.n, 4);
+    const bool vector_ok = (o.n % 4 == 0) && (o.ldc % 4 == 0) &&
+                           (reinterpret_cast<uintptr_t>(o.c) % 8 == 0);
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(static_cast<unsigned>(cdiv(threads, 256)));
+    lc.blockDim = dim3(256);
+    lc.dynamicSmemBytes = 0;
+    lc.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    HST_CUDA(cudaLaunchKernelEx(&lc, splitk_reduce_kernel, static_cast<const float*>(partials),
+                                o.c, o.ldc, o.m, o.n, splits, vector_ok ? 1 : 0));
+  }
+  return HST_OK;
+}
+
+int dispatch_stream(const DeviceState& dev, const Plan& p, const Operands& o, float* partials,
+                    cudaStream_t stream) {
+#define HST_STREAM_CASE(NT_, MP_, BK_)                                                  \
+  if (p.nt == NT_ && p.mp == MP_ && p.bk == BK_)                                        \
+    return launch_stream<NT_, MP_, BK_>(dev, o, p.stages, p.splits, p.kb_per_split, partials, \
+                                        stream);
+  HST_STREAM_CASE(64, 16, 64)
+  HST_STREAM_CASE(64, 32, 64)
+  HST_STREAM_CASE(128, 16, 64)
+  HST_STREAM_CASE(128, 32, 64)
+  HST_STREAM_CASE(128, 64, 64)
+  HST_STREAM_CASE(128, 128, 64)
+  HST_STREAM_CASE(128, 256, 64)
+  HST_STREAM_CASE(128, 16, 128)
+  HST_STREAM_CASE(128, 32, 128)
+  HST_STREAM_CASE(128, 64, 128)
+  HST_STREAM_CASE(128, 128, 128)
+  HST_STREAM_CASE(128, 256, 128)
+#undef HST_STREAM_CASE
+  return fail(HST_ERR_UNSUPPORTED, "no stream kernel for UMMA M %d, N %d, K %d", p.nt, p.mp,
+              p.bk);
+}
+
+// ------------------------------------------------------------------------------------------
+// Common GEMM driver
+// ------------------------------------------------------------------------------------------
+
+int check_problem(const void* a, const void* b, const void* c, int64_t m, int64_t n, int64_t k,
+                  int64_t ldc) {
+  if (m < 0 || n < 0 || k < 0) return fail(HST_ERR_INVALID, "negative matrix extent");
+  if (m > INT32_MAX / 2 || n > INT32_MAX / 2 || k > INT32_MAX / 2)
+    return fail(HST_ERR_INVALID, "matrix extent too large");
+  if (m > 0 && n > 0) {
+    if (c == nullptr) return fail(HST_ERR_INVALID, "output pointer is null");
+    if (ldc < n) return fail(HST_ERR_INVALID, "ldc %lld < n %lld", (long long)ldc, (long long)n);
+    if (k > 0 && (a == nullptr || b == nullptr))
+      return fail(HST_ERR_INVALID, "input pointer is null");
+  }
+  return HST_OK;
+}
+
+int gemm_impl(const hst_gemm_config* cfg, const void* a, int64_t sa0, int64_t sa1, const void* b,
+              int64_t sb0, int64_t sb1, void* c, int64_t ldc, int64_t m, int64_t n, int64_t k,
+              void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  HST_TRY(check_problem(a, b, c, m, n, k, ldc));
+  DeviceState* dev = nullptr;
+  HST_TRY(device_state(&dev));
+  const View va{static_cast<const __half*>(a), m, k, sa0, sa1};
+  const View vb{static_cast<const __half*>(b), k, n, sb0, sb1};
+  Plan p;
+  HST_TRY(make_plan(cfg, va, vb, m, n, k, dev->sm_count, &p));
+  if (m == 0 || n == 0) return HST_OK;
+  __half* cc = static_cast<__half*>(c);
+  if (k == 0) {
+    fill_zero_fp16_kernel<<<grid_for(m * n, dev->sm_count), 256, 0, stream>>>(cc, ldc, m, n);
+    HST_CUDA(cudaGetLastError());
+    return HST_OK;
+  }
+  if (workspace_bytes < p.total || (p.total > 0 && workspace == nullptr))
+    return fail(HST_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu required",
+                workspace_bytes, p.total);
+  if (p.total > 0 && (reinterpret_cast<uintptr_t>(workspace) % kAlign) != 0)
+    return fail(HST_ERR_INVALID, "workspace must be %zu-byte aligned", kAlign);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+
+  Operands o;
+  o.m = static_cast<int>(m);
+  o.n = static_cast<int>(n);
+  o.k = static_cast<int>(k);
+  if (p.pack_a) {
+    __half* dst = reinterpret_cast<__half*>(ws + p.off_a);
+    pack_fp16_kernel<<<grid_for(m * p.lda_p, dev->sm_count), 256, 0, stream>>>(
+        va.ptr, sa0, sa1, m, k, dst, p.lda_p);
+    HST_CUDA(cudaGetLastError());
+    o.a = dst;
+    o.lda = p.lda_p;
+  } else {
+    o.a = va.ptr;
+    o.lda = tma_row_stride(va);
+  }
+  if (p.pack_b) {
+    __half* dst = reinterpret_cast<__half*>(ws + p.off_b);
+    pack_fp16_kernel<<<grid_for(k * p.ldb_p, dev->sm_count), 256, 0, stream>>>(
+        vb.ptr, sb0, sb1, k, n, dst, p.ldb_p);
+    HST_CUDA(cudaGetLastError());
+    o.b = dst;
+    o.ldb = p.ldb_p;
+  } else {
+    o.b = vb.ptr;
+    o.ldb = tma_row_stride(vb);
+  }
+
+  if (p.family == HST_FAMILY_SPLIT_K || p.family == HST_FAMILY_STREAM) {
+    o.c = cc;
+    o.ldc = ldc;
+    float* partials = reinterpret_cast<float*>(ws + p.off_p);
+    return dispatch_stream(*dev, p, o, partials, stream);
+  }
+
+  // Tile and persistent kernels store C with TMA: 16-byte aligned rows, else a padded copy.
+  const bool direct_c = !p.c_tmp && (ldc % 8 == 0) && (reinterpret_cast<uintptr_t>(c) % 16 == 0);
+  if (direct_c) {
+    o.c = cc;
+    o.ldc = ldc;
+  } else {
+    if (!p.c_tmp) {
+      // Aligned N but an unaligned destination: fall back to the padded staging buffer. The plan
+      // did not reserve it, so ask the caller for more workspace.
+      return fail(HST_ERR_INVALID, "output rows must be 16-byte aligned (ldc %% 8 == 0)");
+    }
+    o.c = reinterpret_cast<__half*>(ws + p.off_c);
+    o.ldc = p.ldc_p;
+  }
+  HST_TRY(dispatch_tile(*dev, p, o, p.family == HST_FAMILY_PERSISTENT, stream));
+  if (!direct_c) {
+    copy_fp16_2d_kernel<<<grid_for(m * n, dev->sm_count), 256, 0, stream>>>(o.c, o.ldc, m, n, cc,
+                                                                            ldc);
+    HST_CUDA(cudaGetLastError());
+  }
+  return HST_OK;
+}
+
+}  // namespace
+}  // namespace hst
+
+// ============================================================================================
+// extern "C"
+// ============================================================================================
+
+using namespace hst;
+
+extern "C" {
+
+int hst_abi_version(void) { return HST_ABI_VERSION; }
+
+const char* hst_last_error(void) { return t_error.c_str(); }
+
+int hst_device_sm_count(int device, int* sm_count) {
+  if (sm_count == nullptr) return fail(HST_ERR_INVALID, "sm_count is null");
+  HST_CUDA(cudaDeviceGetAttribute(sm_count, cudaDevAttrMultiProcessorCount, device));
+  return HST_OK;
+}
+
+int hst_gemm_workspace_size(const hst_gemm_config* config, const void* a, int64_t a_stride0,
+                            int64_t a_stride1, const void* b, int64_t b_stride0,
+                            int64_t b_stride1, int64_t m, int64_t n, int64_t k, int device,
+                            size_t* bytes) {
+  if (bytes == nullptr) return fail(HST_ERR_INVALID, "bytes is null");
+  int sms = 0;
+  HST_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  const View va{static_cast<const __half*>(a), m, k, a_stride0, a_stride1};
+  const View vb{static_cast<const __half*>(b), k, n, b_stride0, b_stride1};
+  Plan p;
+  HST_TRY(make_plan(config, va, vb, m, n, k, sms, &p));
+  *bytes = (m == 0 || n == 0 || k == 0) ? 0 : p.total;
+  return HST_OK;
+}
+
+int hst_gemm(const hst_gemm_config* config, const void* a, int64_t a_stride0, int64_t a_stride1,
+             const void* b, int64_t b_stride0, int64_t b_stride1, void* c, int64_t ldc,
+             int64_t m, int64_t n, int64_t k, void* workspace, size_t workspace_bytes,
+             void* stream) {
+  return gemm_impl(config, a, a_stride0, a_stride1, b, b_stride0, b_stride1, c, ldc, m, n, k,
+                   workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int hst_matmul_tile(int32_t block_m, int32_t block_n, int32_t block_k, int32_t num_warps,
+                    int32_t num_stages, int32_t group_m, const void* a, int64_t a_stride0,
+                    int64_t a_stride1, const void* b, int64_t b_stride0, int64_t b_stride1,
+                    void* c, int64_t ldc, int64_t m, int64_t n, int64_t k, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  const hst_gemm_config cfg{HST_FAMILY_TILE, block_m, block_n, block_k, num_warps, num_stages,
+                            group_m, 0};
+  return gemm_impl(&cfg, a, a_stride0, a_stride1, b, b_stride0, b_stride1, c, ldc, m, n, k,
+                   workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int hst_matmul_persistent(int32_t block_m, int32_t block_n, int32_t block_k, int32_t num_warps,
+                          int32_t num_stages, int32_t group_m, const void* a, const void* b,
+                          void* c, int64_t m, int64_t n, int64_t k, void* stream) {
+  if (k % 8 != 0 || n % 8 != 0)
+    return fail(HST_ERR_INVALID,
+                "tensor descriptors require 16-byte aligned leading strides: K=%lld and N=%lld "
+                "must both be multiples of 8",
+                static_cast<long long>(k), static_cast<long long>(n));
+  const hst_gemm_config cfg{HST_FAMILY_PERSISTENT, block_m, block_n, block_k, num_warps,
+                            num_stages, group_m, 0};
+  return gemm_impl(&cfg, a, k, 1, b, n, 1, c, n, m, n, k, nullptr, 0,
+                   static_cast<cudaStream_t>(stream));
+}
+
+int hst_matmul_split_k(int32_t block_m, int32_t block_n, int32_t block_k, int32_t num_warps,
+                       int32_t num_stages, int32_t split_k, const void* a, int64_t a_stride0,
+                       int64_t a_stride1, const void* b, int64_t b_stride0, int64_t b_stride1,
+                       void* c, int64_t ldc, int64_t m, int64_t n, int64_t k, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  const hst_gemm_config cfg{HST_FAMILY_SPLIT_K, block_m, block_n, block_k, num_warps,
+                            num_stages, 8, split_k};
+  return gemm_impl(&cfg, a, a_stride0, a_stride1, b, b_stride0, b_stride1, c, ldc, m, n, k,
+                   workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int hst_matmul_stream(int32_t block_m, int32_t block_k, int32_t num_stages, int32_t split_k,
+                      const void* a, int64_t a_stride0, int64_t a_stride1, const void* b,
+                      int64_t b_stride0, int64_t b_stride1, void* c, int64_t ldc, int64_t m,
+                      int64_t n, int64_t k, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  const hst_gemm_config cfg{HST_FAMILY_STREAM, block_m, 128, block_k, 4, num_stages, 8, split_k};
+  return gemm_impl(&cfg, a, a_stride0, a_stride1, b, b_stride0, b_stride1, c, ldc, m, n, k,
+                   workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int hst_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* y, int64_t ldy,
+                int64_t rows, int64_t hidden, float eps, void* stream) {
+  if (rows < 0 || hidden < 1) return fail(HST_ERR_INVALID, "rows must be >= 0 and hidden >= 1");
+  if (rows > INT32_MAX) return fail(HST_ERR_INVALID, "too many rows");
+  if (ldx < hidden || ldy < hidden) return fail(HST_ERR_INVALID, "row strides must be >= hidden");
+  if (!(eps >= 0.f)) return fail(HST_ERR_INVALID, "eps must be non-negative");
+  if (rows == 0) return HST_OK;
+  if (x == nullptr || gamma == nullptr || y == nullptr)
+    return fail(HST_ERR_INVALID, "null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const __half* xp = static_cast<const __half*>(x);
+  const __half* gp = static_cast<const __half*>(gamma);
+  __half* yp = static_cast<__half*>(y);
+  const bool aligned = hidden % 8 == 0 && ldx % 8 == 0 && ldy % 8 == 0 &&
+                       (reinterpret_cast<uintptr_t>(x) % 16) == 0 &&
+                       (reinterpret_cast<uintptr_t>(gamma) % 16) == 0 &&
+                       (reinterpret_cast<uintptr_t>(y) % 16) == 0;
+  const int64_t vecs = hidden / 8;
+  const int h = static_cast<int>(hidden);
+  if (aligned && vecs <= 256 * 16) {
+    int chunks = 1;
+    while (cdiv(vecs, chunks) > 256) chunks *= 2;
+    const int threads = static_cast<int>(round_up(cdiv(vecs, chunks), 32));
+    const dim3 grid(static_cast<unsigned>(rows));
+    switch (chunks) {
+      case 1: rmsnorm_vec_kernel<1><<<grid, threads, 0, s>>>(xp, gp, yp, h, ldx, ldy, eps); break;
+      case 2: rmsnorm_vec_kernel<2><<<grid, threads, 0, s>>>(xp, gp, yp, h, ldx, ldy, eps); break;
+      case 4: rmsnorm_vec_kernel<4><<<grid, threads, 0, s>>>(xp, gp, yp, h, ldx, ldy, eps); break;
+      case 8: rmsnorm_vec_kernel<8><<<grid, threads, 0, s>>>(xp, gp, yp, h, ldx, ldy, eps); break;
+      default: rmsnorm_vec_kernel<16><<<grid, threads, 0, s>>>(xp, gp, yp, h, ldx, ldy, eps); break;
+    }
+  } else {
+    rmsnorm_scalar_kernel<<<static_cast<unsigned>(rows), 256, 0, s>>>(xp, gp, yp, h, ldx, ldy, eps);
+  }
+  HST_CUDA(cudaGetLastError());
+  return HST_OK;
+}
+
+int hst_status(int device, int* bits, int clear) {
+  if (bits == nullptr) return fail(HST_ERR_INVALID, "bits is null");
+  int prev = 0;
+  HST_CUDA(cudaGetDevice(&prev));
+  HST_CUDA(cudaSetDevice(device));
+  DeviceState* dev = nullptr;
+  int rc = device_state(&dev);
+  if (rc == HST_OK) {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(bits, dev->status, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && clear) e = cudaMemset(dev->status, 0, sizeof(int));
+    if (e != cudaSuccess) rc = fail(HST_ERR_CUDA, "reading the status word failed: %s", cudaGetErrorString(e));
+  }
+  cudaSetDevice(prev);
+  return rc;
+}
+
+int hst_probe_wait_timeout(uint64_t limit_ns, void* stream) {
+  DeviceState* dev = nullptr;
+  HST_TRY(device_state(&dev));
+  if (limit_ns > 1000000000ull) return fail(HST_ERR_INVALID, "probe limit above one second");
+  probe_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(dev->status, limit_ns);
+  HST_CUDA(cudaGetLastError());
+  return HST_OK;
+}
+
+}  // extern "C"

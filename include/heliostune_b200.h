@@ -1,0 +1,130 @@
+/*
+ * heliostune_b200 -- C ABI of the B200 FP16 matmul path.
+ *
+ * Plain pointers, 64-bit sizes and strides (in elements), a CUDA stream passed as void*.
+ * Every entry point returns HST_OK or an HST_ERR_* code; hst_last_error() gives the message of
+ * the calling thread's last failure. No entry point allocates device memory: outputs and
+ * workspaces are the caller's (the Python layer allocates them with torch, per call, as the
+ * reference does). Launches are asynchronous on the given stream; nothing synchronises.
+ *
+ * Each GEMM entry point replaces one reference launcher (file:line in mottopanikeiku/heliostune):
+ *   hst_matmul_tile        <- heliostune.kernel.matmul                     src/heliostune/kernel.py:83
+ *   hst_matmul_persistent  <- heliostune.hopper_kernel.hopper_matmul      src/heliostune/hopper_kernel.py:250
+ *   hst_matmul_split_k     <- heliostune.action_expansion._split_k_matmul src/heliostune/action_expansion.py:124
+ *   hst_gemm               <- heliostune.action_expansion.launch          src/heliostune/action_expansion.py:176
+ *   hst_rmsnorm            <- heliostune_fusion_v2::residual_rmsnorm      src/heliostune/_fusion_gpu.py:76
+ * hst_matmul_stream has no reference counterpart (B200 weight-streaming family, M <= 256).
+ */
+#ifndef HELIOSTUNE_B200_H_
+#define HELIOSTUNE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HST_ABI_VERSION 1
+
+/* Return codes. INVALID and UNSUPPORTED map to ValueError, CUDA and TIMEOUT to RuntimeError. */
+#define HST_OK 0
+#define HST_ERR_INVALID 1      /* bad shape, stride, pointer or configuration value */
+#define HST_ERR_UNSUPPORTED 2  /* a configuration this library has no kernel for */
+#define HST_ERR_WORKSPACE 3    /* the workspace given is smaller than hst_gemm_workspace_size */
+#define HST_ERR_CUDA 4         /* a CUDA runtime or driver call failed */
+#define HST_ERR_TIMEOUT 5      /* a kernel's bounded wait ran out (see hst_status) */
+
+/* Candidate families, as ActionCandidate.family in src/heliostune/action_configs.py:70-77. */
+#define HST_FAMILY_TILE 0       /* KernelConfig        -> tcgen05 tile GEMM, one CTA per tile */
+#define HST_FAMILY_PERSISTENT 1 /* HopperGemmConfig    -> persistent tcgen05 GEMM, grid = #SMs */
+#define HST_FAMILY_SPLIT_K 2    /* SplitKConfig        -> swap-AB split-K + fixed-order reduce */
+#define HST_FAMILY_STREAM 3     /* StreamConfig        -> swap-AB weight streaming, M <= 256 */
+
+/* Field names and meaning follow the reference's config dataclasses
+ * (configs.py:11-51, configs.py:269-356, action_configs.py:20-59). group_m is ignored by the
+ * split-K and stream families; split_k by the tile and persistent families (0 = automatic for
+ * the stream family). */
+typedef struct hst_gemm_config {
+  int32_t family;
+  int32_t block_m;
+  int32_t block_n;
+  int32_t block_k;
+  int32_t num_warps;
+  int32_t num_stages;
+  int32_t group_m;
+  int32_t split_k;
+} hst_gemm_config;
+
+int hst_abi_version(void);
+
+/* Message of the calling thread's last failed call (empty string if none). */
+const char* hst_last_error(void);
+
+/* Number of SMs of a device (148 on a B200). */
+int hst_device_sm_count(int device, int* sm_count);
+
+/* Bytes of workspace hst_gemm needs for these operands: FP32 split-K partials, plus packed
+ * copies of operands whose layout a TMA tensor map cannot describe (unit inner stride,
+ * 16-byte aligned base and row stride). a and b are only inspected for alignment. */
+int hst_gemm_workspace_size(const hst_gemm_config* config, const void* a, int64_t a_stride0,
+                            int64_t a_stride1, const void* b, int64_t b_stride0,
+                            int64_t b_stride1, int64_t m, int64_t n, int64_t k, int device,
+                            size_t* bytes);
+
+/* C[m, n] (row stride ldc, unit column stride) = A[m, k] * B[k, n], FP16 in and out, FP32
+ * accumulation. A and B may have any strides. Replaces action_expansion.launch. */
+int hst_gemm(const hst_gemm_config* config, const void* a, int64_t a_stride0, int64_t a_stride1,
+             const void* b, int64_t b_stride0, int64_t b_stride1, void* c, int64_t ldc,
+             int64_t m, int64_t n, int64_t k, void* workspace, size_t workspace_bytes,
+             void* stream);
+
+/* Tile family (kernel.py:83-118). */
+int hst_matmul_tile(int32_t block_m, int32_t block_n, int32_t block_k, int32_t num_warps,
+                    int32_t num_stages, int32_t group_m, const void* a, int64_t a_stride0,
+                    int64_t a_stride1, const void* b, int64_t b_stride0, int64_t b_stride1,
+                    void* c, int64_t ldc, int64_t m, int64_t n, int64_t k, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* Persistent family (hopper_kernel.py:250-290): A and B row-major contiguous, K % 8 == 0 and
+ * N % 8 == 0, as the reference requires of its tensor descriptors. */
+int hst_matmul_persistent(int32_t block_m, int32_t block_n, int32_t block_k, int32_t num_warps,
+                          int32_t num_stages, int32_t group_m, const void* a, const void* b,
+                          void* c, int64_t m, int64_t n, int64_t k, void* stream);
+
+/* Split-K family (action_expansion.py:124-173): 1 <= m <= 31, any strides; the FP32 partials
+ * [split_k][m][n] live in the workspace. */
+int hst_matmul_split_k(int32_t block_m, int32_t block_n, int32_t block_k, int32_t num_warps,
+                       int32_t num_stages, int32_t split_k, const void* a, int64_t a_stride0,
+                       int64_t a_stride1, const void* b, int64_t b_stride0, int64_t b_stride1,
+                       void* c, int64_t ldc, int64_t m, int64_t n, int64_t k, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* B200 weight-streaming family (no reference counterpart): 1 <= m <= 256; split_k = 0 chooses
+ * the split that fills the SMs. */
+int hst_matmul_stream(int32_t block_m, int32_t block_k, int32_t num_stages, int32_t split_k,
+                      const void* a, int64_t a_stride0, int64_t a_stride1, const void* b,
+                      int64_t b_stride0, int64_t b_stride1, void* c, int64_t ldc, int64_t m,
+                      int64_t n, int64_t k, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/* y[r, :] = fp16((x[r, :] * rsqrt(mean(x[r, :]^2) + eps)) * gamma), FP32 row sum.
+ * Replaces the residual RMSNorm op (_fusion_gpu.py:49-94) in the form measured here: FP16,
+ * no residual, caller-chosen eps. */
+int hst_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* y, int64_t ldy,
+                int64_t rows, int64_t hidden, float eps, void* stream);
+
+/* Status word of a device: bits set by kernels whose bounded waits ran out (1 producer,
+ * 2 UMMA issuer, 4 epilogue, 8 drain, 16 timeout probe). Synchronises the device.
+ * clear != 0 resets it afterwards. */
+int hst_status(int device, int* bits, int clear);
+
+/* Test hook for the failure path: launches one CTA that waits on an mbarrier nobody arrives at,
+ * bounded by limit_ns; when the bound runs out the kernel sets status bit 16 and returns. */
+int hst_probe_wait_timeout(uint64_t limit_ns, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HELIOSTUNE_B200_H_ */

@@ -1,0 +1,175 @@
+"""Frozen candidate manifests: the reference's own tests (tests/test_action_configs.py:21-120)
+ported onto heliostune_b200, plus equality with the manifests the reference itself emits."""
+
+from __future__ import annotations
+
+import subprocess
+import sys
+from dataclasses import FrozenInstanceError, replace
+
+import pytest
+
+from heliostune_b200.action_configs import (
+    ALL_CANDIDATES,
+    NON_SPLIT_CANDIDATES,
+    SPLIT_K_CANDIDATES,
+    ActionCandidate,
+    SplitKConfig,
+    StreamConfig,
+    action_set_manifest,
+    b200_candidates_for,
+    candidates_for,
+    split_plan,
+    stream_block_m,
+    stream_candidates_for,
+    stream_splits,
+)
+from heliostune_b200.configs import (
+    DEFAULT_CONFIGS,
+    DEFAULT_WORKLOADS,
+    EDGE_WORKLOADS,
+    GRID_WORKLOADS,
+    SWEEP_WORKLOADS,
+    HopperGemmConfig,
+    KernelConfig,
+    Workload,
+)
+from heliostune_b200.errors import SchemaError
+from tests.conftest import ROOT, load_golden
+
+
+def test_enumeration_does_not_import_gpu_dependencies() -> None:
+    code = (
+        "import sys; "
+        "from heliostune_b200.action_configs import candidates_for, b200_candidates_for; "
+        "from heliostune_b200.configs import DEFAULT_WORKLOADS, GRID_WORKLOADS; "
+        "assert all(candidates_for(w) for w in DEFAULT_WORKLOADS); "
+        "assert all(b200_candidates_for(w) for w in GRID_WORKLOADS); "
+        "import heliostune_b200.bandit, heliostune_b200.tuner; "
+        "assert 'torch' not in sys.modules; "
+        "assert 'heliostune_b200.action_expansion' not in sys.modules"
+    )
+    subprocess.run([sys.executable, "-c", code], check=True, cwd=ROOT)
+
+
+def test_exact_non_split_candidates_are_frozen() -> None:
+    tiles = {c.config for c in NON_SPLIT_CANDIDATES if c.family == "tile"}
+    persistent = {c.config for c in NON_SPLIT_CANDIDATES if c.family == "persistent"}
+    assert tiles == {
+        KernelConfig(128, 128, 64, 4, 5),
+        KernelConfig(128, 256, 64, 8, 4),
+        KernelConfig(256, 128, 64, 8, 4),
+        KernelConfig(128, 128, 128, 8, 3),
+    }
+    assert persistent == {HopperGemmConfig(128, 128, 64, 4, 4), HopperGemmConfig(128, 256, 64, 8, 3)}
+    assert len(NON_SPLIT_CANDIDATES) == 6
+
+
+def test_exact_split_candidates_are_frozen() -> None:
+    assert {c.config for c in SPLIT_K_CANDIDATES} == {
+        SplitKConfig(16, 64, 64, 4, 3, 4),
+        SplitKConfig(16, 64, 64, 4, 3, 16),
+        SplitKConfig(16, 128, 64, 4, 3, 4),
+        SplitKConfig(16, 128, 64, 4, 3, 16),
+    }
+
+
+def test_every_workload_gets_only_its_applicable_candidates() -> None:
+    assert len(DEFAULT_WORKLOADS) == 96
+    for workload in DEFAULT_WORKLOADS:
+        candidates = candidates_for(workload)
+        assert candidates is (ALL_CANDIDATES if workload.m <= 31 else NON_SPLIT_CANDIDATES)
+    edge = replace(DEFAULT_WORKLOADS[0], m=32)
+    assert candidates_for(edge) is NON_SPLIT_CANDIDATES
+    assert candidates_for(replace(edge, m=31)) is ALL_CANDIDATES
+
+
+def test_candidate_ids_are_sorted_unique_and_disjoint_from_old_actions() -> None:
+    keys = tuple(c.key for c in ALL_CANDIDATES)
+    assert keys == tuple(sorted(keys))
+    assert len(set(keys)) == 10
+    assert set(keys).isdisjoint(c.key for c in DEFAULT_CONFIGS)
+    for candidate in ALL_CANDIDATES:
+        assert candidate.key == f"{candidate.family}:{candidate.config.key}"
+        assert candidate.to_dict() == candidate.config.to_dict()
+
+
+def test_candidates_are_immutable() -> None:
+    candidate = SPLIT_K_CANDIDATES[0]
+    with pytest.raises(FrozenInstanceError):
+        candidate.config = candidate.config  # type: ignore[misc]
+    with pytest.raises(TypeError):
+        ActionCandidate("m16")  # type: ignore[arg-type]
+
+
+@pytest.mark.parametrize(
+    "fields",
+    [
+        dict(block_m=24),
+        dict(block_m=8),
+        dict(split_k=1),
+        dict(split_k=3),
+        dict(num_warps=3),
+        dict(block_n=True),
+    ],
+)
+def test_split_k_config_validation(fields: dict[str, object]) -> None:
+    base = dict(block_m=16, block_n=64, block_k=64, num_warps=4, num_stages=3, split_k=4)
+    base.update(fields)
+    with pytest.raises(SchemaError):
+        SplitKConfig(**base)  # type: ignore[arg-type]
+
+
+def test_manifests_match_the_reference() -> None:
+    golden = load_golden("manifest.json")
+    assert action_set_manifest() == golden["action_set"]
+    assert [c.key for c in ALL_CANDIDATES] == golden["all_candidate_keys"]
+    assert [c.key for c in DEFAULT_CONFIGS] == golden["default_config_keys"]
+    assert [[w.key, w.m, w.n, w.k, w.flops] for w in DEFAULT_WORKLOADS] == golden["default_workloads"]
+    assert [w.key for w in EDGE_WORKLOADS] == golden["edge_workloads"]
+    assert {w.key: [c.key for c in candidates_for(w)] for w in DEFAULT_WORKLOADS} == golden[
+        "candidates_by_workload"
+    ]
+
+
+def test_config_round_trips() -> None:
+    for config in DEFAULT_CONFIGS:
+        assert KernelConfig.from_dict(config.to_dict()) == config
+    persistent = HopperGemmConfig(128, 256, 64, 8, 3)
+    assert HopperGemmConfig.from_dict(persistent.to_dict()) == persistent
+    for workload in GRID_WORKLOADS[:5]:
+        assert Workload.from_dict(workload.to_dict()) == workload
+    with pytest.raises(SchemaError):
+        KernelConfig.from_dict({"block_m": 16})
+
+
+def test_measurement_grids() -> None:
+    assert len(GRID_WORKLOADS) == 96
+    assert len({w.key for w in GRID_WORKLOADS}) == 96
+    assert sorted({(w.k, w.n) for w in GRID_WORKLOADS}) == sorted(
+        [(4096, 6144), (4096, 4096), (4096, 28672), (14336, 4096), (3584, 4608), (3584, 3584),
+         (3584, 37888), (18944, 3584)]
+    )
+    assert sorted({w.m for w in GRID_WORKLOADS}) == [1, 2, 4, 8, 16, 31, 32, 64, 128, 512, 2048, 8192]
+    assert len(SWEEP_WORKLOADS) == 28
+
+
+def test_stream_family() -> None:
+    assert stream_block_m(1) == 16 and stream_block_m(17) == 32 and stream_block_m(256) == 256
+    w = GRID_WORKLOADS[0]
+    assert all(c.family == "stream" for c in stream_candidates_for(w))
+    assert stream_candidates_for(replace(w, m=512)) == ()
+    assert set(candidates_for(w)) <= set(b200_candidates_for(w))
+    with pytest.raises(SchemaError):
+        StreamConfig(16, 64, 64, 4, 8, 0)
+    # The automatic split fills 148 SMs without exceeding one wave of CTAs.
+    config = StreamConfig(16, 128, 64, 4, 8, 0)
+    splits = stream_splits(1, 3584, 18944, config, 148)
+    assert 28 * splits <= 148 and 28 * (splits + 1) > 148
+
+
+def test_split_plan_matches_the_reference_interval_rule() -> None:
+    # tiles_per_split = cdiv(cdiv(K, BK), S); splits past K are dropped.
+    assert split_plan(1543, 64, 16) == (2, 13)
+    assert split_plan(17, 64, 16) == (1, 1)
+    assert split_plan(18944, 64, 4) == (74, 4)

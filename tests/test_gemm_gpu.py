@@ -1,0 +1,228 @@
+"""GPU parity of every GEMM family against the FP32 reference and the CPU oracle.
+
+The first three tests are the reference's own GPU tests (tests/test_action_expansion.py:43-82)
+on the B200 API; the rest add the edge shapes, the stock configurations, the B200 streaming
+family, the golden fixtures through the C ABI, full-size shapes of the measured grid, bitwise
+run-to-run reproducibility, no input mutation, and an error no worse than cuBLAS's."""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from heliostune_b200 import _native
+from heliostune_b200.action_configs import (
+    ALL_CANDIDATES,
+    NON_SPLIT_CANDIDATES,
+    SPLIT_K_CANDIDATES,
+    ActionCandidate,
+    StreamConfig,
+    stream_block_m,
+    stream_candidates_for,
+)
+from heliostune_b200.action_expansion import fp32_reference, launch
+from heliostune_b200.configs import DEFAULT_CONFIGS, EDGE_WORKLOADS, GRID_WORKLOADS, KernelConfig, Workload
+from heliostune_b200.kernel import matmul
+from oracle import oracle
+from tests.conftest import GOLDEN
+from tests.gpu_helpers import assert_gemm_parity, normwise, require_cuda, scaled_normal
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _cuda() -> None:
+    require_cuda()
+    _native.library()
+
+
+@pytest.mark.parametrize("candidate", SPLIT_K_CANDIDATES, ids=lambda c: c.key)
+@pytest.mark.parametrize("m", (1, 7, 31))
+@pytest.mark.parametrize("k", (17, 1543))
+def test_split_k_masks_edges_and_empty_splits(candidate: ActionCandidate, m: int, k: int) -> None:
+    torch.manual_seed(17)
+    a = torch.rand((m, k), device="cuda", dtype=torch.float16)
+    b = torch.rand((k, 131), device="cuda", dtype=torch.float16)
+    assert_gemm_parity(launch(a, b, candidate), a, b)
+
+
+@pytest.mark.parametrize("candidate", SPLIT_K_CANDIDATES, ids=lambda c: c.key)
+def test_split_k_supports_strided_inputs(candidate: ActionCandidate) -> None:
+    torch.manual_seed(31)
+    a = torch.rand((31, 514), device="cuda", dtype=torch.float16)[:, ::2]
+    b = torch.rand((514, 134), device="cuda", dtype=torch.float16)[::2, ::2]
+    assert not a.is_contiguous() and not b.is_contiguous()
+    assert_gemm_parity(launch(a, b, candidate), a, b)
+
+
+@pytest.mark.parametrize("candidate", NON_SPLIT_CANDIDATES, ids=lambda c: c.key)
+@pytest.mark.parametrize("m", (1, 7, 31, 257))
+def test_frozen_tile_and_persistent_candidates_match_reference(candidate: ActionCandidate, m: int) -> None:
+    torch.manual_seed(257)
+    a = torch.rand((m, 256), device="cuda", dtype=torch.float16)
+    b = torch.rand((256, 256), device="cuda", dtype=torch.float16)
+    assert_gemm_parity(launch(a, b, candidate), a, b)
+
+
+@pytest.mark.parametrize("workload", EDGE_WORKLOADS, ids=lambda w: w.projection)
+@pytest.mark.parametrize("candidate", ALL_CANDIDATES, ids=lambda c: c.key)
+def test_edge_workloads(workload: Workload, candidate: ActionCandidate) -> None:
+    if candidate.family == "split_k" and workload.m > 31:
+        pytest.skip("split-K is defined for M <= 31")
+    g = torch.Generator(device="cuda").manual_seed(workload.m * 7 + workload.n)
+    a = scaled_normal((workload.m, workload.k), workload.k, g)
+    b = scaled_normal((workload.k, workload.n), workload.k, g)
+    assert_gemm_parity(launch(a, b, candidate), a, b)
+
+
+@pytest.mark.parametrize("config", DEFAULT_CONFIGS, ids=lambda c: c.key)
+@pytest.mark.parametrize("shape", ((100, 264, 136), (37, 131, 77)), ids=("aligned", "odd"))
+def test_stock_tile_configurations(config: KernelConfig, shape: tuple[int, int, int]) -> None:
+    m, n, k = shape
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    a = scaled_normal((m, k), k, g)
+    b = scaled_normal((k, n), k, g)
+    assert_gemm_parity(matmul(a, b, config), a, b)
+
+
+@pytest.mark.parametrize("m", (1, 2, 16, 17, 31, 32, 64, 100, 128, 200, 256))
+def test_stream_family(m: int) -> None:
+    k, n = 4096, 4096
+    workload = Workload(m=m, n=n, k=k, model="t", projection="t", regime="t")
+    g = torch.Generator(device="cuda").manual_seed(m)
+    a = scaled_normal((m, k), k, g)
+    b = scaled_normal((k, n), k, g)
+    candidates = stream_candidates_for(workload)
+    assert candidates
+    for candidate in candidates:
+        assert_gemm_parity(launch(a, b, candidate), a, b)
+    fixed = ActionCandidate(StreamConfig(stream_block_m(m), 128, 64, 4, 4, 3))
+    assert_gemm_parity(launch(a, b, fixed), a, b)
+
+
+def _abi_gemm(config: _native.GemmConfig, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Call hst_gemm of the C ABI directly with device buffers."""
+    lib = _native.library()
+    m, k = a.shape
+    n = b.shape[1]
+    size = ctypes.c_size_t()
+    _native.check(
+        lib.hst_gemm_workspace_size(
+            ctypes.byref(config), a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(), b.stride(0),
+            b.stride(1), m, n, k, torch.cuda.current_device(), ctypes.byref(size),
+        )
+    )
+    ws = torch.empty(max(size.value, 1), dtype=torch.uint8, device="cuda")
+    c = torch.empty((m, n), dtype=torch.float16, device="cuda")
+    _native.check(
+        lib.hst_gemm(
+            ctypes.byref(config), a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(), b.stride(0),
+            b.stride(1), c.data_ptr(), n, m, n, k, ws.data_ptr(), size.value,
+            torch.cuda.current_stream().cuda_stream,
+        )
+    )
+    torch.cuda.synchronize()
+    return c
+
+
+GOLDEN_CASES = ("edge_1x8x8", "edge_7x136x264", "edge_131x1032x520", "splitk_7x131x17", "splitk_31x131x1543")
+ABI_CONFIGS = {
+    "tile": _native.GemmConfig(_native.FAMILY_TILE, 128, 128, 64, 4, 5, 8, 0),
+    "tile256": _native.GemmConfig(_native.FAMILY_TILE, 256, 128, 64, 8, 4, 8, 0),
+    "persistent": _native.GemmConfig(_native.FAMILY_PERSISTENT, 128, 256, 64, 8, 3, 8, 0),
+    "split_k": _native.GemmConfig(_native.FAMILY_SPLIT_K, 16, 128, 64, 4, 3, 8, 16),
+    "stream": _native.GemmConfig(_native.FAMILY_STREAM, 256, 128, 64, 4, 4, 8, 0),
+}
+
+
+@pytest.mark.parametrize("name", GOLDEN_CASES)
+@pytest.mark.parametrize("family", list(ABI_CONFIGS))
+def test_golden_fixtures_through_the_c_abi(name: str, family: str) -> None:
+    cases = np.load(GOLDEN / "gemm_cases.npz")
+    a_np, b_np = cases[f"{name}_a"], cases[f"{name}_b"]
+    m = a_np.shape[0]
+    if family == "split_k" and m > 31 or family == "stream" and m > 256:
+        pytest.skip("outside the family's M range")
+    a = torch.from_numpy(a_np).cuda()
+    b = torch.from_numpy(b_np).cuda()
+    out = _abi_gemm(ABI_CONFIGS[family], a, b).cpu().numpy()
+    rows = cases[f"{name}_crows"]
+    expected = cases[f"{name}_c"]
+    assert oracle.within_tolerance(out[rows], expected, atol=1e-2, rtol=1e-2)
+    assert oracle.normwise_error(out[rows], expected) <= 1e-2
+    # and against the oracle on every row
+    full = oracle.gemm_fp32_reference(a_np, b_np)
+    assert oracle.normwise_error(out, full) <= 1e-2
+
+
+def test_strided_golden_fixture_through_the_c_abi() -> None:
+    cases = np.load(GOLDEN / "gemm_cases.npz")
+    a = torch.from_numpy(cases["strided_a_full"]).cuda()[:, ::2]
+    b = torch.from_numpy(cases["strided_b_full"]).cuda()[::2, ::2]
+    for family in ("tile", "split_k", "stream"):
+        out = _abi_gemm(ABI_CONFIGS[family], a, b).cpu().numpy()
+        assert oracle.within_tolerance(out, cases["strided_c"], atol=1e-2, rtol=1e-2)
+
+
+FULL_SIZE = (
+    (GRID_WORKLOADS[-1].__class__(m=1, n=3584, k=18944, model="qwen2.5-7b", projection="ffn-down", regime="m1")),
+    Workload(m=31, n=37888, k=3584, model="qwen2.5-7b", projection="ffn-gate-up", regime="m31"),
+    Workload(m=128, n=28672, k=4096, model="llama-3-8b", projection="ffn-gate-up", regime="m128"),
+    Workload(m=2048, n=6144, k=4096, model="llama-3-8b", projection="attention-qkv", regime="m2048"),
+)
+
+
+@pytest.mark.parametrize("workload", FULL_SIZE, ids=lambda w: w.key)
+def test_full_size_grid_shapes(workload: Workload) -> None:
+    from heliostune_b200.action_configs import b200_candidates_for
+
+    g = torch.Generator(device="cuda").manual_seed(workload.m)
+    a = scaled_normal((workload.m, workload.k), workload.k, g)
+    b = scaled_normal((workload.k, workload.n), workload.k, g)
+    expected = fp32_reference(a, b)
+    cublas_error = normwise(torch.matmul(a, b), expected)
+    for candidate in b200_candidates_for(workload):
+        out = launch(a, b, candidate)
+        error = assert_gemm_parity(out, a, b)
+        # no worse than cuBLAS torch.matmul on the same inputs
+        assert error <= 1.25 * cublas_error + 2.0**-14, (candidate.key, error, cublas_error)
+
+
+@pytest.mark.parametrize(
+    "candidate",
+    [
+        ActionCandidate(KernelConfig(128, 256, 64, 8, 4)),
+        ActionCandidate(KernelConfig(64, 64, 64, 4, 2)),
+        *[c for c in ALL_CANDIDATES if c.family in ("persistent", "split_k")][:3],
+        ActionCandidate(StreamConfig(32, 128, 64, 4, 8, 0)),
+    ],
+    ids=lambda c: c.key,
+)
+def test_bitwise_reproducible_and_inputs_untouched(candidate: ActionCandidate) -> None:
+    m = 31 if candidate.family in ("split_k", "stream") else 300
+    k, n = 4096, 3584
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = scaled_normal((m, k), k, g)
+    b = scaled_normal((k, n), k, g)
+    a0, b0 = a.clone(), b.clone()
+    first = launch(a, b, candidate)
+    for _ in range(3):
+        again = launch(a, b, candidate)
+        assert torch.equal(first.view(torch.int16), again.view(torch.int16))
+    assert torch.equal(a.view(torch.int16), a0.view(torch.int16))
+    assert torch.equal(b.view(torch.int16), b0.view(torch.int16))
+
+
+def test_empty_and_degenerate_extents() -> None:
+    a = torch.zeros((0, 64), device="cuda", dtype=torch.float16)
+    b = torch.zeros((64, 32), device="cuda", dtype=torch.float16)
+    assert launch(a, b, NON_SPLIT_CANDIDATES[0]).shape == (0, 32)
+    a = torch.zeros((5, 0), device="cuda", dtype=torch.float16)
+    b = torch.zeros((0, 16), device="cuda", dtype=torch.float16)
+    out = matmul(a, b, KernelConfig(128, 128, 64, 4, 5))
+    assert out.shape == (5, 16) and bool((out == 0).all())
+    with pytest.raises(ValueError, match="split-K requires"):
+        launch(torch.zeros((32, 64), device="cuda", dtype=torch.float16), torch.zeros((64, 16), device="cuda", dtype=torch.float16), SPLIT_K_CANDIDATES[0])

@@ -1,0 +1,98 @@
+"""The C-ABI boundary without a GPU: the header and the built library agree, the library loads,
+and the Python layer rejects bad calls before any CUDA work."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+
+import pytest
+import torch
+
+from heliostune_b200 import _native
+from heliostune_b200.action_configs import NON_SPLIT_CANDIDATES, SPLIT_K_CANDIDATES, SplitKConfig
+from heliostune_b200.configs import HopperGemmConfig, KernelConfig
+
+
+def _declared_symbols() -> set[str]:
+    text = _native.HEADER_PATH.read_text()
+    return set(re.findall(r"^\s*(?:int|const char\*)\s+(hst_\w+)\s*\(", text, flags=re.M))
+
+
+@pytest.fixture(scope="module")
+def lib() -> ctypes.CDLL:
+    _native.build_library()
+    return _native.library()
+
+
+def test_header_declares_exactly_the_exported_entry_points() -> None:
+    assert _declared_symbols() == set(_native.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol(lib: ctypes.CDLL) -> None:
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_native.LIBRARY_PATH)], capture_output=True, text=True, check=True)
+    exported = set(re.findall(r"\sT\s(hst_\w+)$", out.stdout, flags=re.M))
+    assert _declared_symbols() <= exported
+    for name in _declared_symbols():
+        assert hasattr(lib, name)
+
+
+def test_library_is_built_for_sm_100a(lib: ctypes.CDLL) -> None:
+    out = subprocess.run(["cuobjdump", "--list-elf", str(_native.LIBRARY_PATH)], capture_output=True, text=True)
+    assert "sm_100a" in out.stdout
+    assert lib.hst_abi_version() == 1
+    assert lib.hst_last_error() == b""
+
+
+def test_inputs_are_validated_before_any_cuda_work() -> None:
+    from heliostune_b200.action_expansion import _split_k_matmul, launch
+    from heliostune_b200.hopper_kernel import hopper_matmul
+    from heliostune_b200.kernel import matmul
+
+    a = torch.zeros((4, 8), dtype=torch.float16)
+    b = torch.zeros((8, 8), dtype=torch.float16)
+    with pytest.raises(ValueError, match="same CUDA device"):
+        matmul(a, b, KernelConfig(128, 128, 64, 4, 5))
+    with pytest.raises(ValueError, match="two-dimensional"):
+        matmul(a[0], b, KernelConfig(128, 128, 64, 4, 5))
+    with pytest.raises(ValueError, match="incompatible matmul shapes"):
+        hopper_matmul(a, b[:4], HopperGemmConfig(128, 128, 64, 4, 4))
+    # The device is checked before the dtype, in the reference's order (kernel.py:85-92).
+    with pytest.raises(ValueError, match="same CUDA device"):
+        _split_k_matmul(a.float(), b, SplitKConfig(16, 64, 64, 4, 3, 4))
+    with pytest.raises(TypeError, match="unknown action configuration"):
+        launch(a, b, type("Fake", (), {"config": object()})())  # type: ignore[arg-type]
+
+
+@pytest.mark.parametrize(
+    ("family", "entrypoint"),
+    (("tile", "matmul"), ("persistent", "hopper_matmul"), ("split_k", "_split_k_matmul")),
+)
+def test_launch_propagates_failures_without_another_implementation(
+    monkeypatch: pytest.MonkeyPatch, family: str, entrypoint: str
+) -> None:
+    """Port of tests/test_action_expansion.py:85-109 of the reference."""
+    from heliostune_b200 import action_expansion
+
+    candidate = next(c for c in (*NON_SPLIT_CANDIDATES, *SPLIT_K_CANDIDATES) if c.family == family)
+    failure = RuntimeError("requested kernel failed")
+
+    def fail(*args: object) -> None:
+        raise failure
+
+    def forbidden(*args: object) -> None:
+        raise AssertionError("another implementation must not run")
+
+    for name in ("matmul", "hopper_matmul", "_split_k_matmul", "_stream_matmul"):
+        monkeypatch.setattr(action_expansion, name, fail if name == entrypoint else forbidden)
+    with pytest.raises(RuntimeError) as raised:
+        action_expansion.launch(None, None, candidate)  # type: ignore[arg-type]
+    assert raised.value is failure
+
+
+def test_missing_library_fails_loudly(monkeypatch: pytest.MonkeyPatch, tmp_path) -> None:  # type: ignore[no-untyped-def]
+    monkeypatch.setattr(_native, "_library", None)
+    monkeypatch.setattr(_native, "LIBRARY_PATH", tmp_path / "absent.so")
+    with pytest.raises(_native.KernelError, match="not built"):
+        _native.library()

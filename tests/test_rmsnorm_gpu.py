@@ -1,0 +1,57 @@
+"""GPU parity of the RMSNorm kernel against the oracle (small) and the FP32 formula (full size)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from heliostune_b200 import _native
+from heliostune_b200.fusion import load_rmsnorm, rmsnorm
+from oracle import oracle
+from tests.gpu_helpers import require_cuda
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _cuda() -> None:
+    require_cuda()
+    _native.library()
+
+
+def _inputs(rows: int, hidden: int, seed: int) -> tuple[torch.Tensor, torch.Tensor]:
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn((rows, hidden), generator=g, device="cuda").to(torch.float16)
+    gamma = (1.0 + 0.1 * torch.randn((hidden,), generator=g, device="cuda")).to(torch.float16)
+    return x, gamma
+
+
+@pytest.mark.parametrize("shape", ((4, 4096), (1, 8192), (3, 1000), (5, 4104), (2, 40000)))
+def test_matches_the_oracle(shape: tuple[int, int]) -> None:
+    x, gamma = _inputs(*shape, seed=shape[0])
+    y = rmsnorm(x, gamma, 1e-6).cpu().numpy()
+    expected = oracle.rmsnorm_reference(x.cpu().numpy(), gamma.cpu().numpy(), 1e-6)
+    # within one FP16 ulp of the FP64 formula, and almost always the same bits
+    ulp = np.abs(expected.astype(np.float32)) * 2.0**-10 + 2.0**-24
+    assert np.all(np.abs(y.astype(np.float32) - expected.astype(np.float32)) <= ulp)
+    assert np.mean(y.view(np.uint16) == expected.view(np.uint16)) > 0.99
+
+
+@pytest.mark.parametrize("rows", (1, 4096, 65536))
+@pytest.mark.parametrize("hidden", (4096, 8192))
+def test_full_size_against_the_fp32_formula(rows: int, hidden: int) -> None:
+    x, gamma = _inputs(rows, hidden, seed=rows + hidden)
+    x0 = x.clone()
+    y = rmsnorm(x, gamma, 1e-6)
+    xf = x.float()
+    expected = (xf * torch.rsqrt((xf * xf).mean(dim=-1, keepdim=True) + 1e-6) * gamma.float()).to(torch.float16)
+    torch.testing.assert_close(y, expected, atol=1e-5, rtol=2.0**-9)
+    assert torch.equal(rmsnorm(x, gamma, 1e-6).view(torch.int16), y.view(torch.int16))
+    assert torch.equal(x.view(torch.int16), x0.view(torch.int16))
+
+
+def test_registry_is_closed() -> None:
+    assert load_rmsnorm("heliostune_b200::rmsnorm") is rmsnorm
+    with pytest.raises(KeyError):
+        load_rmsnorm("heliostune_fusion_v2::residual_rmsnorm_w4")
