@@ -82,7 +82,7 @@ def _workloads(name: str, shapes: str | None):
 
 class ClockSampler:
     QUERY = (
-        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
     )
@@ -94,7 +94,7 @@ class ClockSampler:
     def __enter__(self) -> ClockSampler:
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "100"],
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "25"],
                 stdout=subprocess.PIPE,
                 stderr=subprocess.DEVNULL,
                 text=True,
@@ -113,19 +113,26 @@ class ClockSampler:
                 self.proc.kill()
                 self.output, _ = self.proc.communicate()
 
-    def summary(self) -> dict[str, object]:
+    def summary(self, start: float | None = None, end: float | None = None) -> dict[str, object]:
+        """Median SM clock and throttle reasons of the samples inside [start, end] (epoch s)."""
+        from datetime import datetime
+
         clocks, max_clock, reasons = [], None, set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         for line in getattr(self, "output", "").splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                clocks.append(float(parts[1]))
-                max_clock = float(parts[2])
+                stamp = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                clock = float(parts[2])
+                max_clock = float(parts[3])
             except ValueError:
                 continue
-            for name, flag in zip(names, parts[5:9], strict=True):
+            if start is not None and not start - 0.03 <= stamp <= end + 0.03:
+                continue
+            clocks.append(clock)
+            for name, flag in zip(names, parts[6:10], strict=True):
                 if flag.lower() == "active":
                     reasons.add(name)
         return {
@@ -211,13 +218,30 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
         return do_bench(lambda: launch(a, b, candidate), warmup_ms=2.0, rep_ms=args.probe_ms, quantiles=(0.5,))[0]
 
     t0 = time.perf_counter()
-    tuning = thompson_probe(workloads, b200_candidates_for, measure, hardware, budget=args.budget, policy_seed=args.seed)
-    tuning_s = time.perf_counter() - t0
     chosen = {}
-    for w in workloads:
-        if w.key not in tuning.recommendations:
-            raise RuntimeError(f"no valid candidate for {w.key}")
-        chosen[w.key] = tuning.recommendations[w.key]
+    if args.force:
+        for w in workloads:
+            by_key = {c.key: c for c in b200_candidates_for(w)}
+            chosen[w.key] = by_key[args.force]
+        from heliostune_b200.tuner import ProbeResult
+
+        tuning = ProbeResult(probes={}, recommendations=dict(chosen))
+    elif args.choices:
+        # Reuse the selection of an earlier run (profiling runs skip the tuning launches).
+        saved = {row["workload"]: row["choice"] for row in json.loads(Path(args.choices).read_text())["shapes"]}
+        for w in workloads:
+            by_key = {c.key: c for c in b200_candidates_for(w)}
+            chosen[w.key] = by_key[saved[w.key]]
+        from heliostune_b200.tuner import ProbeResult
+
+        tuning = ProbeResult(probes={}, recommendations=dict(chosen))
+    else:
+        tuning = thompson_probe(workloads, b200_candidates_for, measure, hardware, budget=args.budget, policy_seed=args.seed)
+        for w in workloads:
+            if w.key not in tuning.recommendations:
+                raise RuntimeError(f"no valid candidate for {w.key}")
+            chosen[w.key] = tuning.recommendations[w.key]
+    tuning_s = time.perf_counter() - t0
     del tune_operands
     torch.cuda.empty_cache()
 
@@ -251,20 +275,23 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
         sampler = ClockSampler(local_rank) if sample_clocks else None
         if sampler:
             sampler.__enter__()
+            time.sleep(0.5)  # nvidia-smi needs a moment before its first sample
         wall0 = time.perf_counter()
+        epoch0 = time.time()
         for s in range(steps):
             one_pass(fn_for, events[s])
         torch.cuda.synchronize()
         wall = time.perf_counter() - wall0
+        epoch1 = time.time()
         if sampler:
             sampler.__exit__(None, None, None)
         if world > 1:
             dist.barrier()
         per_shape = [[events[s][i][0].elapsed_time(events[s][i][1]) for s in range(steps)] for i in range(n)]
-        return per_shape, wall, (sampler.summary() if sampler else None)
+        return per_shape, wall, (sampler.summary(epoch0, epoch1) if sampler else None)
 
     ours_times, ours_wall, clocks = timed(ours_fn, args.steps, args.warmup, sample_clocks=True)
-    cublas_times, _, _ = timed(cublas_fn, args.steps, args.warmup)
+    cublas_times, _, _ = timed(cublas_fn, args.steps, args.warmup) if not args.skip_cublas else (ours_times, 0.0, None)
     ours_ms = [statistics.median(t) for t in ours_times]
     cublas_ms = [statistics.median(t) for t in cublas_times]
     total_flops = sum(w.flops for w in workloads)
@@ -310,7 +337,7 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
 
     roofline = family_roofline(dominant)
     roofline["kernel"] = {"tile": "tile_gemm_kernel", "persistent": "tile_gemm_kernel (persistent grid)", "split_k": "stream_gemm_kernel + splitk_reduce_kernel", "stream": "stream_gemm_kernel"}[dominant]
-    roofline["traffic"] = _traffic_from_profiles(dominant)
+    roofline.update(_traffic_from_profiles(dominant))
 
     # per-shape roofline fraction (slower of tensor and HBM bound)
     shape_frac = []
@@ -319,7 +346,10 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
         shape_frac.append(t_roof / (ms / 1e3))
 
     # ---- 3. end to end through the public API with host buffers ------------------------------
-    e2e_ms, h2d_bytes, d2h_bytes = _e2e_pass(workloads, operands, chosen, device, args.e2e_steps)
+    if args.e2e_steps > 0:
+        e2e_ms, h2d_bytes, d2h_bytes = _e2e_pass(workloads, operands, chosen, device, args.e2e_steps)
+    else:
+        e2e_ms, h2d_bytes, d2h_bytes = list(ours_ms), 0, 0
 
     launches = sum(_launch_count(chosen[w.key], w, sm_count) for w in workloads) * args.steps
 
@@ -402,13 +432,19 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
     return result if rank == 0 else None
 
 
-def _traffic_from_profiles(family: str) -> float | None:
+def _traffic_from_profiles(family: str) -> dict[str, object]:
+    """DRAM bytes of one ncu-captured launch of the family's kernel (profiles/traffic.json),
+    beside the algorithmic bytes of that same launch."""
     path = ROOT / "profiles" / "traffic.json"
-    if not path.exists():
-        return None
-    data = json.loads(path.read_text())
-    entry = data.get(family)
-    return None if entry is None else entry.get("bytes_per_launch")
+    entry = json.loads(path.read_text()).get(family) if path.exists() else None
+    if entry is None:
+        return {"traffic": None}
+    m, n, k = (int(part.split("=")[1]) for part in entry["workload"].split())
+    return {
+        "traffic": entry["bytes_per_launch"],
+        "traffic_launch": f"{entry['kernel']} at {entry['workload']}",
+        "traffic_algorithmic_bytes": 2 * (m * k + k * n + m * n),
+    }
 
 
 def _e2e_pass(workloads, operands, chosen, device, steps: int):
@@ -527,7 +563,7 @@ def run_reference(args: argparse.Namespace) -> dict[str, object] | None:
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=5)
+    parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--workload", choices=("grid", "sweep", "decode", "colpar"), default="grid")
@@ -540,6 +576,9 @@ def main() -> None:
     parser.add_argument("--cpu-budget-s", type=float, default=20.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--detail", action="store_true", help="write per-shape results under gpurun_out/")
+    parser.add_argument("--choices", default=None, help="per-shape choices from an earlier --detail file")
+    parser.add_argument("--skip-cublas", action="store_true", help="profiling runs: no cuBLAS passes")
+    parser.add_argument("--force", default=None, help="profiling runs: one candidate key for every shape")
     args = parser.parse_args()
     if args.warmup < 3 and args.impl == "ours" and not args.shapes:
         print("note: fewer than 3 warm-up passes", file=sys.stderr)
