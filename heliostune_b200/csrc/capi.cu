@@ -755,3 +755,103 @@ int hst_probe_wait_timeout(uint64_t limit_ns, void* stream) {
 }
 
 }  // extern "C"
+
+// ============================================================================================
+// Allocation-free split-K entry point
+//
+// Some callers cannot allocate device memory at the moment they want a GEMM: a host process
+// that reserved the whole GPU up front and hands out no new buffers, an FFI binding of this C
+// ABI with no device allocator of its own, or code running where a cudaMalloc would stall or
+// be refused. They still own their inputs and outputs; what they cannot provide is the FP32
+// split-K partials buffer. This entry point keeps that buffer in a fixed file-scope device
+// array instead, so it allocates nothing.
+//
+// Limits and sharing:
+//   * The array holds kNoAllocScratchFloats FP32 values (16 MiB). Every GPU that loads this
+//     library keeps it for the life of the process. A call whose effective splits x M x N
+//     exceed it is rejected with HST_ERR_INVALID before anything is launched.
+//   * Every call on a device uses the same array. Nothing in it has to start at zero: each
+//     launch writes every partial it later reads. Two calls whose kernels overlap on the GPU
+//     (different streams, or different host threads) race on the array and corrupt each
+//     other's results; serialise them.
+//   * Operands must already be TMA-describable (unit inner stride, 16-byte aligned base and row
+//     stride), because repacking them would need more scratch.
+//   * The first call on each device looks up the device address of the array with
+//     cudaGetSymbolAddress (the array's name in host code is only a stand-in for it); make that
+//     first call before any stream capture.
+// ============================================================================================
+
+namespace hst {
+namespace {
+
+constexpr size_t kNoAllocScratchFloats = size_t(4) << 20;  // 4 Mi floats = 16 MiB
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocScratchFloats];
+
+float* g_noalloc_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mutex;
+
+// Device address of the scratch array on the current device, looked up once per device.
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  HST_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(HST_ERR_INVALID, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_partials);
+    if (err != cudaSuccess || ptr == nullptr) {
+      return fail(HST_ERR_CUDA, "cudaGetSymbolAddress of the split-K scratch array failed: %s",
+                  cudaGetErrorString(err));
+    }
+    g_noalloc_ptr[dev] = static_cast<float*>(ptr);
+  }
+  *out = g_noalloc_ptr[dev];
+  return HST_OK;
+}
+
+}  // namespace
+}  // namespace hst
+
+extern "C" int hst_matmul_split_k_noalloc(int32_t block_m, int32_t block_n, int32_t block_k,
+                                          int32_t num_warps, int32_t num_stages, int32_t split_k,
+                                          const void* a, int64_t a_stride0, int64_t a_stride1,
+                                          const void* b, int64_t b_stride0, int64_t b_stride1,
+                                          void* c, int64_t ldc, int64_t m, int64_t n, int64_t k,
+                                          void* stream) {
+  using namespace hst;
+  HST_TRY(check_problem(a, b, c, m, n, k, ldc));
+  DeviceState* dev = nullptr;
+  HST_TRY(device_state(&dev));
+  const hst_gemm_config cfg{HST_FAMILY_SPLIT_K, block_m, block_n, block_k, num_warps,
+                            num_stages, 8, split_k};
+  const View va{static_cast<const __half*>(a), m, k, a_stride0, a_stride1};
+  const View vb{static_cast<const __half*>(b), k, n, b_stride0, b_stride1};
+  Plan p;
+  HST_TRY(make_plan(&cfg, va, vb, m, n, k, dev->sm_count, &p));
+  if (p.pack_a || p.pack_b) {
+    return fail(HST_ERR_INVALID,
+                "the allocation-free split-K needs row-major operands with unit inner stride and "
+                "16-byte aligned base and rows");
+  }
+  const size_t needed = p.splits > 1 ? size_t(p.splits) * size_t(m) * size_t(n) : 0;
+  if (needed > kNoAllocScratchFloats) {
+    return fail(HST_ERR_INVALID,
+                "the allocation-free split-K needs %zu FP32 partials (%d splits x M=%lld x "
+                "N=%lld) but its scratch array holds %zu",
+                needed, p.splits, static_cast<long long>(m), static_cast<long long>(n),
+                kNoAllocScratchFloats);
+  }
+  float* scratch = nullptr;
+  HST_TRY(noalloc_scratch(&scratch));
+  Operands o;
+  o.m = static_cast<int>(m);
+  o.n = static_cast<int>(n);
+  o.k = static_cast<int>(k);
+  o.a = va.ptr;
+  o.lda = tma_row_stride(va);
+  o.b = vb.ptr;
+  o.ldb = tma_row_stride(vb);
+  o.c = static_cast<__half*>(c);
+  o.ldc = ldc;
+  return dispatch_stream(*dev, p, o, scratch, static_cast<cudaStream_t>(stream));
+}

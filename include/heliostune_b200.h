@@ -119,6 +119,21 @@ int hst_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* y, int64_t 
  * clear != 0 resets it afterwards. */
 int hst_status(int device, int* bits, int clear);
 
+/* Allocation-free split-K (no counterpart in the reference). For callers that cannot allocate
+ * device memory when they call -- a process that reserved the whole GPU up front, or an FFI
+ * caller with no device allocator -- but still own A, B and C. The FP32 partials live in a
+ * fixed 16 MiB device array inside this library instead of a caller workspace, so nothing is
+ * allocated. Same arguments and result as hst_matmul_split_k without the workspace; operands
+ * must be row-major with 16-byte aligned rows. Rejects (HST_ERR_INVALID) calls whose
+ * splits x M x N partials exceed 4 Mi floats. All calls on a device share the array: calls
+ * that overlap on the GPU race and must be serialised. The first call on a device looks up the
+ * array's device address; make it before any stream capture. */
+int hst_matmul_split_k_noalloc(int32_t block_m, int32_t block_n, int32_t block_k,
+                               int32_t num_warps, int32_t num_stages, int32_t split_k,
+                               const void* a, int64_t a_stride0, int64_t a_stride1, const void* b,
+                               int64_t b_stride0, int64_t b_stride1, void* c, int64_t ldc,
+                               int64_t m, int64_t n, int64_t k, void* stream);
+
 /* Test hook for the failure path: launches one CTA that waits on an mbarrier nobody arrives at,
  * bounded by limit_ns; when the bound runs out the kernel sets status bit 16 and returns. */
 int hst_probe_wait_timeout(uint64_t limit_ns, void* stream);
