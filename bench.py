@@ -432,6 +432,111 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
     return result if rank == 0 else None
 
 
+def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
+    """Config 5: C[M, N] = A[M, K] B[K, N] with B split N-wise over the ranks, each rank's
+    slice computed by the B200 GEMM, NCCL all-gather of the slices, column assembly."""
+    import torch
+    import torch.distributed as dist
+
+    from heliostune_b200 import _native
+    from heliostune_b200.column_parallel import COLUMN_PARALLEL_CANDIDATE, ColumnShard, column_parallel_matmul
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    _native.library()
+    (w,) = _workloads("colpar", args.shapes)
+    shard = ColumnShard(w.n, world, rank)
+    g = torch.Generator(device=device).manual_seed(5)
+    a = (torch.randn((w.m, w.k), generator=g, device=device) / math.sqrt(w.k)).to(torch.float16)
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    b_shard = (torch.randn((w.k, shard.cols), generator=g, device=device) / math.sqrt(w.k)).to(torch.float16)
+
+    def step(events):
+        return column_parallel_matmul(a, b_shard, phase_events=events)
+
+    for _ in range(args.warmup):
+        step(None)
+    torch.cuda.synchronize()
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local_rank)
+    sampler.__enter__()
+    time.sleep(0.5)
+    epoch0 = time.time()
+    for s_ in range(args.steps):
+        out = step(events[s_])
+        del out
+    torch.cuda.synchronize()
+    epoch1 = time.time()
+    sampler.__exit__(None, None, None)
+    if world > 1:
+        dist.barrier()
+    gemm_ms = statistics.median(e[0].elapsed_time(e[1]) for e in events)
+    gather_ms = statistics.median(e[1].elapsed_time(e[2]) for e in events)
+    step_ms = statistics.median(e[0].elapsed_time(e[2]) for e in events)
+    times = torch.tensor([step_ms, gemm_ms, gather_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    step_ms, gemm_ms, gather_ms = (float(t) for t in times.tolist())
+    peaks, source = _peaks()
+    flops = 2.0 * w.m * w.n * w.k
+    gemm_tflops = flops / world / (gemm_ms / 1e3) / 1e12
+    gather_bytes = 2.0 * w.m * w.n * (world - 1) / world
+    # Roofline of the whole step: the slower of the per-GPU GEMM at the tensor peak and the
+    # all-gather bytes every GPU receives at the measured 770 GB/s peer bandwidth.
+    t_roof = max(flops / world / (peaks["bf16_tflops_sustained"] * 1e12), gather_bytes / 770e9)
+    result: dict[str, object] = {
+        "metric": "column-parallel FP16 GEMM M=8192 K=8192 N=57344: TFLOP/s (whole job)",
+        "value": round(flops / (step_ms / 1e3) / 1e12, 3),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f16 (fp32 accumulate)",
+        "data": "synthetic: seeded N(0,1)/sqrt(K) FP16 operands",
+        "config": {
+            "workload": f"colpar M={w.m} N={w.n} K={w.k}",
+            "parallelism": f"column-parallel x{world}",
+            "gemm": COLUMN_PARALLEL_CANDIDATE.key,
+            "l2": "operands larger than L2",
+        },
+        "gemm_ms": round(gemm_ms, 4),
+        "gather_ms": round(gather_ms, 4),
+        "roofline": {
+            "bound": "tensor",
+            "achieved": round(gemm_tflops, 2),
+            "peak": peaks["bf16_tflops_sustained"],
+            "unit": "TFLOP/s",
+            "frac": round(gemm_tflops / peaks["bf16_tflops_sustained"], 4),
+            "peak_source": f"{source} (sustained)",
+            "kernel": "tile_gemm_kernel<128,1,256,64> (GEMM phase, per GPU)",
+            "traffic": None,
+        },
+        "step_roofline_frac": round(t_roof / (step_ms / 1e3), 4),
+        "gather_gbs": round(gather_bytes / (gather_ms / 1e3) / 1e9, 1) if world > 1 else None,
+        "gpu_launches": 2 * args.steps,
+        "clocks": sampler.summary(epoch0, epoch1),
+        "status_bits": _native.status(local_rank),
+    }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result if rank == 0 else None
+
+
 def _traffic_from_profiles(family: str) -> dict[str, object]:
     """DRAM bytes of one ncu-captured launch of the family's kernel (profiles/traffic.json),
     beside the algorithmic bytes of that same launch."""
@@ -582,7 +687,12 @@ def main() -> None:
     args = parser.parse_args()
     if args.warmup < 3 and args.impl == "ours" and not args.shapes:
         print("note: fewer than 3 warm-up passes", file=sys.stderr)
-    result = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if args.impl == "reference":
+        result = run_reference(args)
+    elif args.workload == "colpar":
+        result = run_colpar(args)
+    else:
+        result = run_ours(args)
     if result is not None:
         print(json.dumps(result), flush=True)
 

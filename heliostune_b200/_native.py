@@ -56,6 +56,7 @@ EXPORTED_SYMBOLS = (
     "hst_status",
     "hst_probe_wait_timeout",
     "hst_matmul_split_k_noalloc",
+    "hst_column_assemble",
 )
 
 
@@ -136,6 +137,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         ),
         "hst_status": ([ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int], ctypes.c_int),
         "hst_probe_wait_timeout": ([_u64, _ptr], ctypes.c_int),
+        "hst_column_assemble": ([_ptr, _ptr, _i64, _i64, _i64, _i64, _ptr], ctypes.c_int),
         "hst_matmul_split_k_noalloc": (
             [_i32] * 6 + [_ptr, _i64, _i64, _ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i64, _ptr],
             ctypes.c_int,

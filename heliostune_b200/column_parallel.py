@@ -1,0 +1,122 @@
+"""Column-parallel (N-sharded) GEMM across the GPUs of one node, joined by an all-gather.
+
+No reference counterpart: the reference has no multi-GPU code. Rank ``r`` of ``P`` holds the
+replicated A ``[M, K]`` and the column slice ``B[:, r*N/P : (r+1)*N/P]``; it computes its slice
+``C_r = A @ B_r`` with the B200 GEMM, the slices are all-gathered over NVLink (NCCL), and
+``hst_column_assemble`` writes the rank-ordered ``[P, M, N/P]`` chunks into the columns of a
+row-major ``C [M, N]``. Every rank ends with the full C. Each GEMM is a single-GPU launch on
+local memory; no TMA load in this library reads another GPU's memory or feeds several CTAs.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from heliostune_b200 import _native
+from heliostune_b200.action_configs import ActionCandidate
+from heliostune_b200.configs import KernelConfig
+
+#: The GEMM configuration each rank uses for its slice (large M, wide N).
+COLUMN_PARALLEL_CANDIDATE = ActionCandidate(KernelConfig(128, 256, 64, 8, 4))
+
+
+@dataclass(frozen=True)
+class ColumnShard:
+    """The columns of C (and of B) rank ``rank`` of ``world`` owns."""
+
+    n_total: int
+    world: int
+    rank: int
+
+    def __post_init__(self) -> None:
+        if self.world < 1 or not 0 <= self.rank < self.world:
+            raise ValueError("rank must be in [0, world)")
+        if self.n_total < 1 or self.n_total % self.world:
+            raise ValueError(f"N={self.n_total} must split evenly over {self.world} ranks")
+
+    @property
+    def cols(self) -> int:
+        return self.n_total // self.world
+
+    @property
+    def start(self) -> int:
+        return self.rank * self.cols
+
+    @property
+    def stop(self) -> int:
+        return self.start + self.cols
+
+    def take(self, b: torch.Tensor) -> torch.Tensor:
+        """This rank's slice of a full ``B [K, N]`` as a contiguous ``[K, N/P]`` tensor."""
+        return b[:, self.start : self.stop].contiguous()
+
+
+def assemble_columns(gathered: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``out[:, p*Nc:(p+1)*Nc] = gathered[p]`` on the GPU (``hst_column_assemble``)."""
+    if gathered.ndim != 3 or gathered.dtype != torch.float16 or not gathered.is_contiguous():
+        raise ValueError("gathered must be a contiguous FP16 [parts, rows, cols] tensor")
+    parts, rows, cols = gathered.shape
+    if out is None:
+        out = torch.empty((rows, parts * cols), dtype=torch.float16, device=gathered.device)
+    if out.shape != (rows, parts * cols) or out.stride(1) != 1:
+        raise ValueError("out must be [rows, parts * cols] with unit column stride")
+    with torch.cuda.device(gathered.device):
+        _native.check(
+            _native.library().hst_column_assemble(
+                gathered.data_ptr(),
+                out.data_ptr(),
+                parts,
+                rows,
+                cols,
+                out.stride(0),
+                torch.cuda.current_stream(gathered.device).cuda_stream,
+            )
+        )
+    return out
+
+
+def _default_gemm(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    from heliostune_b200.action_expansion import launch
+
+    return launch(a, b, COLUMN_PARALLEL_CANDIDATE)
+
+
+def column_parallel_matmul(
+    a: torch.Tensor,
+    b_shard: torch.Tensor,
+    *,
+    group: dist.ProcessGroup | None = None,
+    gemm: Callable[[torch.Tensor, torch.Tensor], torch.Tensor] | None = None,
+    assemble: Callable[[torch.Tensor], torch.Tensor] | None = None,
+    phase_events: list[torch.cuda.Event] | None = None,
+) -> torch.Tensor:
+    """Full ``C = A @ B`` on every rank from this rank's column slice of B.
+
+    ``gemm`` and ``assemble`` default to the B200 kernels; tests on CPU ranks pass host
+    implementations to exercise the sharding and gather logic. ``phase_events`` (three CUDA
+    events) are recorded before the GEMM, after the GEMM and after the assembly, so callers can
+    time the two phases on the launching stream.
+    """
+    gemm = gemm or _default_gemm
+    assemble = assemble or assemble_columns
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if phase_events:
+        phase_events[0].record()
+    local = gemm(a, b_shard)
+    if phase_events:
+        phase_events[1].record()
+    if world == 1:
+        gathered = local.unsqueeze(0)
+    else:
+        rows, cols = local.shape
+        flat = torch.empty((world * rows, cols), dtype=local.dtype, device=local.device)
+        dist.all_gather_into_tensor(flat, local.contiguous(), group=group)
+        gathered = flat.view(world, rows, cols)
+    out = assemble(gathered)
+    if phase_events:
+        phase_events[2].record()
+    return out

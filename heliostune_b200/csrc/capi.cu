@@ -202,6 +202,29 @@ __global__ void fill_zero_fp16_kernel(__half* __restrict__ dst, int64_t ldd, int
   }
 }
 
+// dst[r, p * cols + c] = src[p][r][c]: puts the rank-ordered chunks an all-gather returns into
+// the columns of a row-major C. Eight halves (16 bytes) per thread when rows are aligned.
+__global__ void column_assemble_kernel(const __half* __restrict__ src, __half* __restrict__ dst,
+                                       int64_t parts, int64_t rows, int64_t cols, int64_t ldd,
+                                       int vec8) {
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  if (vec8) {
+    const int64_t vcols = cols / 8;
+    const int64_t total = parts * rows * vcols;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += step) {
+      const int64_t v = i % vcols, r = (i / vcols) % rows, p = i / (vcols * rows);
+      const uint4 x = __ldcs(reinterpret_cast<const uint4*>(src) + i);
+      __stcs(reinterpret_cast<uint4*>(dst + r * ldd + p * cols) + v, x);
+    }
+  } else {
+    const int64_t total = parts * rows * cols;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += step) {
+      const int64_t c = i % cols, r = (i / cols) % rows, p = i / (cols * rows);
+      dst[r * ldd + p * cols + c] = src[i];
+    }
+  }
+}
+
 __global__ void probe_timeout_kernel(int* status, uint64_t limit_ns) {
   __shared__ uint64_t bar;
   __shared__ int abort_flag;
@@ -724,6 +747,25 @@ int hst_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* y, int64_t 
   } else {
     rmsnorm_scalar_kernel<<<static_cast<unsigned>(rows), 256, 0, s>>>(xp, gp, yp, h, ldx, ldy, eps);
   }
+  HST_CUDA(cudaGetLastError());
+  return HST_OK;
+}
+
+int hst_column_assemble(const void* src, void* dst, int64_t parts, int64_t rows,
+                        int64_t cols_per_part, int64_t ldd, void* stream) {
+  if (parts < 1 || rows < 0 || cols_per_part < 0) return fail(HST_ERR_INVALID, "negative extent");
+  if (ldd < parts * cols_per_part) return fail(HST_ERR_INVALID, "ldd smaller than parts x cols");
+  if (rows == 0 || cols_per_part == 0) return HST_OK;
+  if (src == nullptr || dst == nullptr) return fail(HST_ERR_INVALID, "null pointer");
+  DeviceState* dev = nullptr;
+  HST_TRY(device_state(&dev));
+  const bool vec8 = cols_per_part % 8 == 0 && ldd % 8 == 0 &&
+                    reinterpret_cast<uintptr_t>(src) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(dst) % 16 == 0;
+  const int64_t work = parts * rows * (vec8 ? cols_per_part / 8 : cols_per_part);
+  column_assemble_kernel<<<grid_for(work, dev->sm_count), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(src), static_cast<__half*>(dst), parts, rows, cols_per_part, ldd,
+      vec8 ? 1 : 0);
   HST_CUDA(cudaGetLastError());
   return HST_OK;
 }

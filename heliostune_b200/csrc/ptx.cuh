@@ -97,7 +97,7 @@ __device__ __forceinline__ void raise_abort(int* status, volatile int* abort, in
 }
 
 // ------------------------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor), no multicast anywhere in this library
+// TMA (cp.async.bulk.tensor): every load targets this CTA's own shared memory
 // ------------------------------------------------------------------------------------------
 
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {

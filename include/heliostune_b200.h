@@ -114,6 +114,12 @@ int hst_matmul_stream(int32_t block_m, int32_t block_k, int32_t num_stages, int3
 int hst_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* y, int64_t ldy,
                 int64_t rows, int64_t hidden, float eps, void* stream);
 
+/* Column-parallel assembly (no reference counterpart: the reference has no multi-GPU path).
+ * dst[r, p * cols_per_part + c] = src[p][r][c] for the rank-ordered [parts][rows][cols_per_part]
+ * chunks an all-gather of per-rank C slices returns; dst has row stride ldd. */
+int hst_column_assemble(const void* src, void* dst, int64_t parts, int64_t rows,
+                        int64_t cols_per_part, int64_t ldd, void* stream);
+
 /* Status word of a device: bits set by kernels whose bounded waits ran out (1 producer,
  * 2 UMMA issuer, 4 epilogue, 8 drain, 16 timeout probe). Synchronises the device.
  * clear != 0 resets it afterwards. */

@@ -1,0 +1,95 @@
+"""Column-parallel GEMM: sharding arithmetic and the all-gather layout on world-size-2 gloo
+ranks (CPU, host implementations of the GEMM and the assembly), plus the GPU assembly kernel."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from heliostune_b200.column_parallel import ColumnShard, column_parallel_matmul
+
+
+def _host_gemm(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    return (a.double() @ b.double()).to(torch.float16)
+
+
+def _host_assemble(gathered: torch.Tensor) -> torch.Tensor:
+    parts, rows, cols = gathered.shape
+    return gathered.permute(1, 0, 2).reshape(rows, parts * cols).contiguous()
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank: int, world: int, port: int, queue) -> None:  # type: ignore[no-untyped-def]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(11)
+        m, k, n = 37, 96, 80
+        a = (torch.randn((m, k), generator=g) / k**0.5).to(torch.float16)
+        b = (torch.randn((k, n), generator=g) / k**0.5).to(torch.float16)
+        shard = ColumnShard(n, world, rank)
+        c = column_parallel_matmul(a, shard.take(b), gemm=_host_gemm, assemble=_host_assemble)
+        expected = _host_gemm(a, b)
+        queue.put((rank, bool(torch.equal(c, expected)), tuple(c.shape)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_assemble_the_full_product() -> None:
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    results = [queue.get(timeout=10) for _ in range(world)]
+    assert sorted(r for r, _, _ in results) == [0, 1]
+    for _, equal, shape in results:
+        assert equal and shape == (37, 80)
+
+
+def test_shard_arithmetic() -> None:
+    shards = [ColumnShard(57344, 8, r) for r in range(8)]
+    assert [s.start for s in shards] == [r * 7168 for r in range(8)]
+    assert shards[-1].stop == 57344
+    with pytest.raises(ValueError):
+        ColumnShard(100, 3, 0)
+    with pytest.raises(ValueError):
+        ColumnShard(96, 4, 4)
+    b = torch.arange(4 * 12).reshape(4, 12)
+    parts = [ColumnShard(12, 3, r).take(b) for r in range(3)]
+    assert torch.equal(torch.cat(parts, dim=1), b)
+
+
+@pytest.mark.gpu
+def test_assembly_kernel_and_single_rank_path() -> None:
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA is unavailable")
+    from heliostune_b200.column_parallel import assemble_columns
+    from tests.gpu_helpers import assert_gemm_parity
+
+    for parts, rows, cols in ((4, 33, 64), (3, 5, 7), (8, 128, 7168 // 8)):
+        gathered = torch.randn((parts, rows, cols), device="cuda").to(torch.float16)
+        out = assemble_columns(gathered)
+        assert torch.equal(out, _host_assemble(gathered.cpu()).cuda())
+    g = torch.Generator(device="cuda").manual_seed(3)
+    a = (torch.randn((512, 1024), generator=g, device="cuda") / 32).to(torch.float16)
+    b = (torch.randn((1024, 2048), generator=g, device="cuda") / 32).to(torch.float16)
+    c = column_parallel_matmul(a, b)
+    assert_gemm_parity(c, a, b)
+    assert np.isfinite(c.float().cpu().numpy()).all()
