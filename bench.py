@@ -401,7 +401,7 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
         "status_bits": _native.status(local_rank),
     }
     if args.detail:
-        detail = ROOT / "gpurun_out" / f"bench_detail_{args.workload}.json"
+        detail = ROOT / "gpurun_out" / f"bench_detail_{args.tag or args.workload}.json"
         detail.parent.mkdir(exist_ok=True)
         detail.write_text(
             json.dumps(
@@ -684,6 +684,7 @@ def main() -> None:
     parser.add_argument("--choices", default=None, help="per-shape choices from an earlier --detail file")
     parser.add_argument("--skip-cublas", action="store_true", help="profiling runs: no cuBLAS passes")
     parser.add_argument("--force", default=None, help="profiling runs: one candidate key for every shape")
+    parser.add_argument("--tag", default=None, help="name of the --detail file")
     args = parser.parse_args()
     if args.warmup < 3 and args.impl == "ours" and not args.shapes:
         print("note: fewer than 3 warm-up passes", file=sys.stderr)

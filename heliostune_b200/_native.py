@@ -40,6 +40,7 @@ FAMILY_TILE = 0
 FAMILY_PERSISTENT = 1
 FAMILY_SPLIT_K = 2
 FAMILY_STREAM = 3
+FAMILY_PAIR = 4
 
 #: Every symbol include/heliostune_b200.h declares.
 EXPORTED_SYMBOLS = (
@@ -52,6 +53,7 @@ EXPORTED_SYMBOLS = (
     "hst_matmul_persistent",
     "hst_matmul_split_k",
     "hst_matmul_stream",
+    "hst_matmul_pair",
     "hst_rmsnorm",
     "hst_status",
     "hst_probe_wait_timeout",
@@ -127,6 +129,11 @@ def _declare(lib: ctypes.CDLL) -> None:
             ctypes.c_int,
         ),
         "hst_matmul_stream": (
+            [_i32] * 4 + [_ptr, _i64, _i64, _ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i64,
+                          _ptr, _size, _ptr],
+            ctypes.c_int,
+        ),
+        "hst_matmul_pair": (
             [_i32] * 4 + [_ptr, _i64, _i64, _ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i64,
                           _ptr, _size, _ptr],
             ctypes.c_int,

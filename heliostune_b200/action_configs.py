@@ -120,7 +120,48 @@ class StreamConfig:
         return asdict(self)
 
 
-ActionConfig = KernelConfig | HopperGemmConfig | SplitKConfig | StreamConfig
+@dataclass(frozen=True, slots=True)
+class PairConfig:
+    """B200 CTA-pair GEMM (no reference counterpart): 256 x ``block_n`` tiles per two SMs.
+
+    A cluster of two CTAs shares one ``tcgen05.mma.cta_group::2`` (UMMA M = 256): each CTA
+    loads its 128 rows of A and half of the tile's ``block_n`` columns of B, so each SM moves
+    half the B bytes of a single-SM tile. Persistent over the tiles in ``group_m`` raster order
+    with two TMEM accumulators; ``num_stages`` is the ring depth per CTA. ``num_warps`` is kept
+    for the key (the CTA runs six warps).
+    """
+
+    block_m: int
+    block_n: int
+    block_k: int
+    num_warps: int
+    num_stages: int
+    group_m: int = 8
+
+    def __post_init__(self) -> None:
+        for name in ("block_m", "block_n", "block_k", "num_warps", "num_stages", "group_m"):
+            exact_int(getattr(self, name), context=f"pair config {name}", minimum=1)
+        if self.block_m != 256:
+            raise SchemaError("block_m must be 256 (two SMs x 128 rows)")
+        if self.block_n not in (128, 256):
+            raise SchemaError("block_n must be 128 or 256")
+        if self.block_k not in (64, 128):
+            raise SchemaError("block_k must be 64 or 128")
+        if self.num_warps not in (1, 2, 4, 8):
+            raise SchemaError("num_warps must be one of 1, 2, 4, or 8")
+
+    @property
+    def key(self) -> str:
+        return (
+            f"pair-m{self.block_m}n{self.block_n}k{self.block_k}"
+            f"-w{self.num_warps}s{self.num_stages}g{self.group_m}"
+        )
+
+    def to_dict(self) -> dict[str, int]:
+        return asdict(self)
+
+
+ActionConfig = KernelConfig | HopperGemmConfig | SplitKConfig | StreamConfig | PairConfig
 
 
 @dataclass(frozen=True, slots=True)
@@ -130,18 +171,22 @@ class ActionCandidate:
     config: ActionConfig
 
     def __post_init__(self) -> None:
-        if not isinstance(self.config, KernelConfig | HopperGemmConfig | SplitKConfig | StreamConfig):
-            raise TypeError("candidate config must be a tile, persistent, split-K or stream config")
+        if not isinstance(
+            self.config, KernelConfig | HopperGemmConfig | SplitKConfig | StreamConfig | PairConfig
+        ):
+            raise TypeError("candidate config must be a tile, persistent, split-K, stream or pair config")
 
     @property
-    def family(self) -> Literal["tile", "persistent", "split_k", "stream"]:
+    def family(self) -> Literal["tile", "persistent", "split_k", "stream", "pair"]:
         if isinstance(self.config, KernelConfig):
             return "tile"
         if isinstance(self.config, HopperGemmConfig):
             return "persistent"
         if isinstance(self.config, SplitKConfig):
             return "split_k"
-        return "stream"
+        if isinstance(self.config, StreamConfig):
+            return "stream"
+        return "pair"
 
     @property
     def key(self) -> str:
@@ -205,9 +250,28 @@ def stream_candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:
     )
 
 
+#: Smallest M the CTA-pair family is offered for (one 256-row tile is half empty below).
+PAIR_M_MINIMUM = 129
+
+PAIR_CANDIDATES: tuple[ActionCandidate, ...] = _sorted(
+    (
+        ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8)),
+        ActionCandidate(PairConfig(256, 128, 64, 4, 8, 8)),
+        ActionCandidate(PairConfig(256, 256, 64, 4, 6, 16)),
+    )
+)
+
+
+def pair_candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:
+    """B200 CTA-pair candidates for ``M > 128`` (empty below)."""
+    return PAIR_CANDIDATES if workload.m >= PAIR_M_MINIMUM else ()
+
+
 def b200_candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:
-    """Everything the B200 tuner may probe: the frozen set plus the streaming family."""
-    return _sorted((*candidates_for(workload), *stream_candidates_for(workload)))
+    """Everything the B200 tuner may probe: the frozen set plus the B200 families."""
+    return _sorted(
+        (*candidates_for(workload), *stream_candidates_for(workload), *pair_candidates_for(workload))
+    )
 
 
 def action_set_manifest() -> dict[str, list[dict[str, Any]]]:

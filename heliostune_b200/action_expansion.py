@@ -22,6 +22,7 @@ from heliostune_b200 import _native
 from heliostune_b200.action_collection import ATOL, REP_MS, RTOL, WARMUP_MS, tensor_seed, timing_order
 from heliostune_b200.action_configs import (
     SPLIT_K_M_LIMIT,
+    PairConfig,
     STREAM_M_LIMIT,
     ActionCandidate,
     SplitKConfig,
@@ -124,6 +125,47 @@ def _stream_matmul(a: torch.Tensor, b: torch.Tensor, config: StreamConfig) -> to
     return output
 
 
+def _pair_matmul(a: torch.Tensor, b: torch.Tensor, config: PairConfig) -> torch.Tensor:
+    m, n, k = _validate(a, b)
+    output = torch.empty((m, n), device=a.device, dtype=torch.float16)
+    native = _native.GemmConfig(
+        _native.FAMILY_PAIR,
+        config.block_m,
+        config.block_n,
+        config.block_k,
+        config.num_warps,
+        config.num_stages,
+        config.group_m,
+        0,
+    )
+    workspace, ws_ptr, ws_bytes = _workspace(native, a, b, m, n, k)
+    with torch.cuda.device(a.device):
+        _native.check(
+            _native.library().hst_matmul_pair(
+                config.block_n,
+                config.block_k,
+                config.num_stages,
+                config.group_m,
+                a.data_ptr(),
+                a.stride(0),
+                a.stride(1),
+                b.data_ptr(),
+                b.stride(0),
+                b.stride(1),
+                output.data_ptr(),
+                n,
+                m,
+                n,
+                k,
+                ws_ptr,
+                ws_bytes,
+                _stream(a.device),
+            )
+        )
+    del workspace
+    return output
+
+
 def launch(a: torch.Tensor, b: torch.Tensor, candidate: ActionCandidate) -> torch.Tensor:
     """Allocate and launch exactly the requested action, propagating every failure."""
     config = candidate.config
@@ -135,6 +177,8 @@ def launch(a: torch.Tensor, b: torch.Tensor, candidate: ActionCandidate) -> torc
         return _split_k_matmul(a, b, config)
     if isinstance(config, StreamConfig):
         return _stream_matmul(a, b, config)
+    if isinstance(config, PairConfig):
+        return _pair_matmul(a, b, config)
     raise TypeError("unknown action configuration")
 
 

@@ -11,6 +11,7 @@
 #include <string>
 
 #include "../../include/heliostune_b200.h"
+#include "gemm_pair.cuh"
 #include "gemm_stream.cuh"
 #include "gemm_tile.cuh"
 #include "rmsnorm.cuh"
@@ -314,6 +315,19 @@ int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t 
       p->group_m = cfg->group_m;
       break;
     }
+    case HST_FAMILY_PAIR: {
+      if (cfg->group_m < 1) return fail(HST_ERR_INVALID, "group_m must be positive");
+      if (bm != 256) return fail(HST_ERR_UNSUPPORTED, "pair tiles have block_m 256");
+      if (bn != 128 && bn != 256) return fail(HST_ERR_UNSUPPORTED, "pair block_n must be 128 or 256");
+      if (bk != 64 && bk != 128) return fail(HST_ERR_UNSUPPORTED, "pair block_k must be 64 or 128");
+      p->um = 128;
+      p->ma = 2;
+      p->bn = bn;
+      p->bk = bk;
+      p->stages = cfg->num_stages < 2 ? 2 : (cfg->num_stages > kMaxStages ? kMaxStages : cfg->num_stages);
+      p->group_m = cfg->group_m;
+      break;
+    }
     case HST_FAMILY_SPLIT_K: {
       if (m < 1 || m > 31 || n < 1 || k < 1)
         return fail(HST_ERR_INVALID, "split-K requires 1 <= M <= 31 and positive N and K");
@@ -448,6 +462,60 @@ int dispatch_tile(const DeviceState& dev, const Plan& p, const Operands& o, bool
 #undef HST_TILE_CASE
   return fail(HST_ERR_UNSUPPORTED, "no tile kernel for UMMA M %d x %d atoms, N %d, K %d", p.um,
               p.ma, p.bn, p.bk);
+}
+
+// ------------------------------------------------------------------------------------------
+// CTA-pair launch
+// ------------------------------------------------------------------------------------------
+
+template <int BN, int BK>
+int launch_pair(const DeviceState& dev, const Operands& o, int stages, int group_m,
+                cudaStream_t stream) {
+  using S = PairShape<BN, BK>;
+  static std::atomic<uint64_t> smem_done{0};
+  HST_TRY(allow_smem(pair_gemm_kernel<BN, BK>, smem_done));
+  while (stages > 2 && S::smem_bytes(stages) > kMaxDynamicSmem) --stages;
+  if (S::smem_bytes(stages) > kMaxDynamicSmem)
+    return fail(HST_ERR_UNSUPPORTED, "pair tile 256x%dx%d does not fit shared memory", BN, BK);
+  CUtensorMap ma_, mb_, mc_;
+  HST_TRY(encode_tiled_2d(&ma_, o.a, o.k, o.m, o.lda, 64, 128));
+  HST_TRY(encode_tiled_2d(&mb_, o.b, o.n, o.k, o.ldb, 64, BK));
+  HST_TRY(encode_tiled_2d(&mc_, o.c, o.n, o.m, o.ldc, 64, 32));
+  TileArgs args;
+  args.m = o.m;
+  args.n = o.n;
+  args.k = o.k;
+  args.tiles_m = static_cast<int>(cdiv(o.m, 256));
+  args.tiles_n = static_cast<int>(cdiv(o.n, BN));
+  args.num_tiles = args.tiles_m * args.tiles_n;
+  args.k_blocks = static_cast<int>(cdiv(o.k, BK));
+  args.group_m = group_m;
+  args.stages = stages;
+  args.status = dev.status;
+  const int max_pairs = dev.sm_count / 2;
+  const int pairs = args.num_tiles < max_pairs ? args.num_tiles : max_pairs;
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  lc.blockDim = dim3(kTileThreads);
+  lc.dynamicSmemBytes = S::smem_bytes(stages);
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  HST_CUDA(cudaLaunchKernelEx(&lc, pair_gemm_kernel<BN, BK>, ma_, mb_, mc_, args));
+  return HST_OK;
+}
+
+int dispatch_pair(const DeviceState& dev, const Plan& p, const Operands& o, cudaStream_t stream) {
+  if (p.bn == 256 && p.bk == 64) return launch_pair<256, 64>(dev, o, p.stages, p.group_m, stream);
+  if (p.bn == 128 && p.bk == 64) return launch_pair<128, 64>(dev, o, p.stages, p.group_m, stream);
+  if (p.bn == 256 && p.bk == 128) return launch_pair<256, 128>(dev, o, p.stages, p.group_m, stream);
+  if (p.bn == 128 && p.bk == 128) return launch_pair<128, 128>(dev, o, p.stages, p.group_m, stream);
+  return fail(HST_ERR_UNSUPPORTED, "no pair kernel for N %d, K %d", p.bn, p.bk);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -614,7 +682,11 @@ int gemm_impl(const hst_gemm_config* cfg, const void* a, int64_t sa0, int64_t sa
     o.c = reinterpret_cast<__half*>(ws + p.off_c);
     o.ldc = p.ldc_p;
   }
-  HST_TRY(dispatch_tile(*dev, p, o, p.family == HST_FAMILY_PERSISTENT, stream));
+  if (p.family == HST_FAMILY_PAIR) {
+    HST_TRY(dispatch_pair(*dev, p, o, stream));
+  } else {
+    HST_TRY(dispatch_tile(*dev, p, o, p.family == HST_FAMILY_PERSISTENT, stream));
+  }
   if (!direct_c) {
     copy_fp16_2d_kernel<<<grid_for(m * n, dev->sm_count), 256, 0, stream>>>(o.c, o.ldc, m, n, cc,
                                                                             ldc);
@@ -709,6 +781,15 @@ int hst_matmul_stream(int32_t block_m, int32_t block_k, int32_t num_stages, int3
                       int64_t n, int64_t k, void* workspace, size_t workspace_bytes,
                       void* stream) {
   const hst_gemm_config cfg{HST_FAMILY_STREAM, block_m, 128, block_k, 4, num_stages, 8, split_k};
+  return gemm_impl(&cfg, a, a_stride0, a_stride1, b, b_stride0, b_stride1, c, ldc, m, n, k,
+                   workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int hst_matmul_pair(int32_t block_n, int32_t block_k, int32_t num_stages, int32_t group_m,
+                    const void* a, int64_t a_stride0, int64_t a_stride1, const void* b,
+                    int64_t b_stride0, int64_t b_stride1, void* c, int64_t ldc, int64_t m,
+                    int64_t n, int64_t k, void* workspace, size_t workspace_bytes, void* stream) {
+  const hst_gemm_config cfg{HST_FAMILY_PAIR, 256, block_n, block_k, 4, num_stages, group_m, 0};
   return gemm_impl(&cfg, a, a_stride0, a_stride1, b, b_stride0, b_stride1, c, ldc, m, n, k,
                    workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }

@@ -1,0 +1,271 @@
+// CTA-pair tcgen05 GEMM: C[M,N] = A[M,K] * B[K,N], 256 x BN output tiles per pair of SMs.
+//
+// B200 "pair" family (no reference counterpart; the reference's largest tiles are the
+// 128x256 / 256x128 frozen candidates of action_configs.py:91-96). A cluster of two CTAs on the
+// two SMs of a TPC computes one 256 x BN tile with tcgen05.mma.cta_group::2 (UMMA M = 256):
+//   * CTA r loads its own 128 rows of A and its own BN/2 columns of B for every K block, so
+//     each SM pulls half the B bytes a single-SM 128 x BN tile would;
+//   * both CTAs' TMA loads complete on the leader CTA's (rank 0) stage barrier;
+//   * one thread of the leader issues the UMMAs; they read A and B from both CTAs' shared
+//     memory and accumulate rows 128r..128r+127 in CTA r's TMEM;
+//   * the leader's tcgen05.commit releases each stage in both CTAs (one commit per CTA) and
+//     publishes each finished accumulator to both CTAs' epilogues;
+//   * each CTA drains its own 128 rows x BN columns exactly like the single-SM kernel, and its
+//     epilogue warps report a free accumulator on the leader's barrier.
+// The kernel is persistent: cluster p walks tiles p, p + #pairs, ... in the grouped raster, with
+// two TMEM accumulators so a tile's epilogue overlaps the next tile's main loop.
+// No TMA load here feeds more than one CTA's shared memory.
+#pragma once
+
+#include "gemm_tile.cuh"
+#include "ptx.cuh"
+
+namespace hst {
+
+template <int BN, int BK>
+struct PairShape {
+  static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
+  static_assert(BK == 64 || BK == 128, "BK must be 64 or 128");
+  static constexpr int kHalfN = BN / 2;
+  static constexpr int kAtomsK = BK / 64;
+  static constexpr int kAtomsN = kHalfN / 64;
+  static constexpr int kABoxBytes = 128 * 128;  // 128 rows x 64 k
+  static constexpr int kBBoxBytes = BK * 128;   // BK rows x 64 n
+  static constexpr int kABytes = kAtomsK * kABoxBytes;
+  static constexpr int kBBytes = kAtomsN * kBBoxBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes;  // per CTA
+  static constexpr int kAccCols = BN;
+  static constexpr int kTmemCols = 2 * BN;  // two accumulators
+  static constexpr int kEpilogueBytes = 4 * 2 * kEpilogueStageBytes;
+  static constexpr int kBarrierBytes = 256 + 16 * kMaxStages;
+  static constexpr uint32_t kIdesc = umma_idesc_f16(256, BN, false, true);
+  static constexpr int smem_bytes(int stages) {
+    return 1024 + stages * kStageBytes + kEpilogueBytes + kBarrierBytes;
+  }
+};
+
+template <int BN, int BK>
+__global__ void __launch_bounds__(kTileThreads, 1)
+    pair_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
+                     const __grid_constant__ CUtensorMap map_b,
+                     const __grid_constant__ CUtensorMap map_c, const TileArgs args) {
+  using S = PairShape<BN, BK>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int stages = args.stages;
+  uint8_t* ring = smem;
+  uint8_t* epi = ring + stages * S::kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi + S::kEpilogueBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kMaxStages;
+  uint64_t* tmem_full = bars + 2 * kMaxStages;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint64_t* mma_done = tmem_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const int pair = static_cast<int>(cluster_id_x());
+  const int pairs = static_cast<int>(nclusters_x());
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tmem_full[b], 1);
+      mbar_init(&tmem_empty[b], 8);  // four epilogue warps in each CTA (leader's copy is used)
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    tma_prefetch_map(&map_a);
+    tma_prefetch_map(&map_b);
+    tma_prefetch_map(&map_c);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, S::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before_sync();
+  cluster_sync();  // both CTAs' barriers exist before either signals the other
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    const uint64_t policy = l2_policy_evict_normal();
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t armed_mask = 0, armed_parity = 0;
+    bool ok = true;
+    for (int tile = pair; tile < args.num_tiles && ok; tile += pairs) {
+      int pm, pn;
+      grouped_tile(tile, args.tiles_m, args.tiles_n, args.group_m, pm, pn);
+      const int m0 = pm * 256 + static_cast<int>(rank) * 128;
+      const int n0 = pn * BN + static_cast<int>(rank) * S::kHalfN;
+      for (int kb = 0; kb < args.k_blocks; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+          raise_abort(args.status, abort_flag, kStatusProducerTimeout);
+          ok = false;
+          break;
+        }
+        uint8_t* st = ring + stage * S::kStageBytes;
+        const uint32_t leader_full = map_to_rank(smem_addr(&full[stage]), 0);
+        if (rank == 0) {
+          mbar_arrive_expect_tx(&full[stage], 2 * S::kStageBytes);
+          armed_mask |= 1u << stage;
+          armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+        }
+        const int k0 = kb * BK;
+#pragma unroll
+        for (int ka = 0; ka < S::kAtomsK; ++ka) {
+          tma_load_2d_pair(st + ka * S::kABoxBytes, &map_a, leader_full, k0 + 64 * ka, m0, policy);
+        }
+#pragma unroll
+        for (int na = 0; na < S::kAtomsN; ++na) {
+          tma_load_2d_pair(st + S::kABytes + na * S::kBBoxBytes, &map_b, leader_full,
+                           n0 + 64 * na, k0, policy);
+        }
+        if (++stage == stages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (!ok && rank == 0) {
+      for (int s = 0; s < stages; ++s) {
+        if ((armed_mask & (1u << s)) &&
+            !mbar_wait(&full[s], (armed_parity >> s) & 1u, nullptr, 200000000ull)) {
+          atomicOr(args.status, kStatusDrainTimeout);
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ---------------- UMMA issuer (leader only) ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int tile = pair; tile < args.num_tiles && ok; tile += pairs) {
+      if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort_flag)) {
+        raise_abort(args.status, abort_flag, kStatusMmaTimeout);
+        ok = false;
+        break;
+      }
+      tc_fence_after_sync();
+      const uint32_t d_base = tmem_base + acc * S::kAccCols;
+      for (int kb = 0; kb < args.k_blocks; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag)) {
+          raise_abort(args.status, abort_flag, kStatusMmaTimeout);
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
+        const uint32_t a_base = smem_addr(ring + stage * S::kStageBytes);
+        const uint32_t b_base = a_base + S::kABytes;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t adesc =
+              smem_desc(a_base + (kk >> 2) * S::kABoxBytes + (kk & 3) * 32, 16, 1024);
+          const uint64_t bdesc = smem_desc(b_base + kk * 2048, S::kBBoxBytes, 1024);
+          umma_f16_pair(d_base, adesc, bdesc, S::kIdesc, (kb | kk) != 0);
+        }
+        const uint32_t own_empty = smem_addr(&empty[stage]);
+        umma_commit_pair(own_empty);
+        umma_commit_pair(map_to_rank(own_empty, 1));
+        if (++stage == stages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      const uint32_t own_full = smem_addr(&tmem_full[acc]);
+      umma_commit_pair(own_full);
+      umma_commit_pair(map_to_rank(own_full, 1));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    umma_commit_pair(smem_addr(mma_done));
+    if (!mbar_wait(mma_done, 0, nullptr, 200000000ull)) atomicOr(args.status, kStatusDrainTimeout);
+  } else if (warp >= 2) {
+    // ---------------- epilogue (both CTAs, own 128 rows) ----------------
+    const int quarter = warp & 3;
+    uint8_t* staging = epi + (warp - 2) * 2 * kEpilogueStageBytes;
+    int buf = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = pair; tile < args.num_tiles; tile += pairs) {
+      int pm, pn;
+      grouped_tile(tile, args.tiles_m, args.tiles_n, args.group_m, pm, pn);
+      const int row0 = pm * 256 + static_cast<int>(rank) * 128 + quarter * 32;
+      const int n0 = pn * BN;
+      const bool ready = __all_sync(0xffffffffu, mbar_wait(&tmem_full[acc], acc_phase, abort_flag));
+      if (!ready) {
+        if (lane == 0) raise_abort(args.status, abort_flag, kStatusEpilogueTimeout);
+        break;
+      }
+      tc_fence_after_sync();
+#pragma unroll 1
+      for (int c = 0; c < BN / 64; ++c) {
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                               acc * S::kAccCols + c * 64;
+        uint32_t lo[32], hi[32];
+        tmem_ld_32x32b_x32(taddr, lo);
+        tmem_ld_32x32b_x32(taddr + 32, hi);
+        tmem_ld_wait();
+        uint8_t* dst = staging + buf * kEpilogueStageBytes;
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        const uint32_t row_addr = smem_addr(dst) + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t* src = (j < 4) ? &lo[j * 8] : &hi[(j - 4) * 8];
+          const uint32_t w0 = pack_half2(__uint_as_float(src[0]), __uint_as_float(src[1]));
+          const uint32_t w1 = pack_half2(__uint_as_float(src[2]), __uint_as_float(src[3]));
+          const uint32_t w2 = pack_half2(__uint_as_float(src[4]), __uint_as_float(src[5]));
+          const uint32_t w3 = pack_half2(__uint_as_float(src[6]), __uint_as_float(src[7]));
+          st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), w0, w1, w2, w3);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&map_c, dst, n0 + c * 64, row0);
+          bulk_commit_group();
+        }
+        buf ^= 1;
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0) {
+          mbar_arrive(&tmem_empty[acc]);
+        } else {
+          mbar_arrive_cluster(map_to_rank(smem_addr(&tmem_empty[acc]), 0));
+        }
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before_sync();
+  cluster_sync();  // the leader's UMMAs read the peer's shared memory until here
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc_pair(tmem_base, S::kTmemCols);
+  }
+}
+
+}  // namespace hst

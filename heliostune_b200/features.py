@@ -6,7 +6,8 @@ onto the same six launch fields by :func:`launch_fields`:
 
 * tile / persistent -- the fields as given;
 * split-K -- ``group_m`` carries ``split_k`` (the reference has no raster group for split-K);
-* stream -- ``group_m`` carries the split the launcher will actually use for the shape.
+* stream -- ``group_m`` carries the split the launcher will actually use for the shape;
+* pair -- the fields as given (``block_m`` = 256 rows per two SMs).
 """
 
 from __future__ import annotations
@@ -17,7 +18,7 @@ from typing import NamedTuple
 import numpy as np
 from numpy.typing import NDArray
 
-from heliostune_b200.action_configs import SplitKConfig, StreamConfig, stream_splits
+from heliostune_b200.action_configs import PairConfig, SplitKConfig, StreamConfig, stream_splits
 from heliostune_b200.configs import HopperGemmConfig, KernelConfig, Workload
 from heliostune_b200.schema import HardwareProfile
 
@@ -61,11 +62,11 @@ class LaunchFields(NamedTuple):
 
 def launch_fields(
     workload: Workload,
-    config: KernelConfig | HopperGemmConfig | SplitKConfig | StreamConfig,
+    config: KernelConfig | HopperGemmConfig | SplitKConfig | StreamConfig | PairConfig,
     hardware: HardwareProfile,
 ) -> LaunchFields:
     """Map any candidate configuration onto the six fields the v2 basis reads."""
-    if isinstance(config, KernelConfig | HopperGemmConfig):
+    if isinstance(config, KernelConfig | HopperGemmConfig | PairConfig):
         group = config.group_m
     elif isinstance(config, SplitKConfig):
         group = config.split_k

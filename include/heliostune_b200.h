@@ -40,6 +40,7 @@ extern "C" {
 #define HST_FAMILY_PERSISTENT 1 /* HopperGemmConfig    -> persistent tcgen05 GEMM, grid = #SMs */
 #define HST_FAMILY_SPLIT_K 2    /* SplitKConfig        -> swap-AB split-K + fixed-order reduce */
 #define HST_FAMILY_STREAM 3     /* StreamConfig        -> swap-AB weight streaming, M <= 256 */
+#define HST_FAMILY_PAIR 4       /* PairConfig          -> CTA-pair (cta_group::2) 256 x N tiles */
 
 /* Field names and meaning follow the reference's config dataclasses
  * (configs.py:11-51, configs.py:269-356, action_configs.py:20-59). group_m is ignored by the
@@ -107,6 +108,14 @@ int hst_matmul_stream(int32_t block_m, int32_t block_k, int32_t num_stages, int3
                       int64_t b_stride0, int64_t b_stride1, void* c, int64_t ldc, int64_t m,
                       int64_t n, int64_t k, void* workspace, size_t workspace_bytes,
                       void* stream);
+
+/* B200 CTA-pair family (no reference counterpart): persistent clusters of two CTAs computing
+ * 256 x block_n tiles (block_n 128 or 256) with tcgen05.mma.cta_group::2. Any strides (packed
+ * through the workspace when a TMA tensor map cannot describe them). */
+int hst_matmul_pair(int32_t block_n, int32_t block_k, int32_t num_stages, int32_t group_m,
+                    const void* a, int64_t a_stride0, int64_t a_stride1, const void* b,
+                    int64_t b_stride0, int64_t b_stride1, void* c, int64_t ldc, int64_t m,
+                    int64_t n, int64_t k, void* workspace, size_t workspace_bytes, void* stream);
 
 /* y[r, :] = fp16((x[r, :] * rsqrt(mean(x[r, :]^2) + eps)) * gamma), FP32 row sum.
  * Replaces the residual RMSNorm op (_fusion_gpu.py:49-94) in the form measured here: FP16,

@@ -16,6 +16,8 @@ import torch
 from heliostune_b200 import _native
 from heliostune_b200.action_configs import (
     ALL_CANDIDATES,
+    PAIR_CANDIDATES,
+    PairConfig,
     NON_SPLIT_CANDIDATES,
     SPLIT_K_CANDIDATES,
     ActionCandidate,
@@ -103,6 +105,28 @@ def test_stream_family(m: int) -> None:
     assert_gemm_parity(launch(a, b, fixed), a, b)
 
 
+@pytest.mark.parametrize("candidate", PAIR_CANDIDATES, ids=lambda c: c.key)
+@pytest.mark.parametrize(
+    "shape",
+    ((512, 4096, 4096), (257, 264, 136), (1000, 1032, 520), (131, 8, 8), (2048, 3584, 18944)),
+    ids=lambda s: "x".join(map(str, s)),
+)
+def test_pair_family(candidate: ActionCandidate, shape: tuple[int, int, int]) -> None:
+    m, n, k = shape
+    g = torch.Generator(device="cuda").manual_seed(m + k)
+    a = scaled_normal((m, k), k, g)
+    b = scaled_normal((k, n), k, g)
+    assert_gemm_parity(launch(a, b, candidate), a, b)
+
+
+def test_pair_family_with_strided_operands_and_deep_k() -> None:
+    g = torch.Generator(device="cuda").manual_seed(9)
+    a = scaled_normal((300, 2 * 1540), 1540, g)[:, ::2]
+    b = scaled_normal((1540, 2 * 520), 1540, g)[:, ::2]
+    for config in (PairConfig(256, 256, 128, 4, 3, 8), PairConfig(256, 128, 128, 4, 4, 4)):
+        assert_gemm_parity(launch(a, b, ActionCandidate(config)), a, b)
+
+
 def _abi_gemm(config: _native.GemmConfig, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """Call hst_gemm of the C ABI directly with device buffers."""
     lib = _native.library()
@@ -135,6 +159,7 @@ ABI_CONFIGS = {
     "persistent": _native.GemmConfig(_native.FAMILY_PERSISTENT, 128, 256, 64, 8, 3, 8, 0),
     "split_k": _native.GemmConfig(_native.FAMILY_SPLIT_K, 16, 128, 64, 4, 3, 8, 16),
     "stream": _native.GemmConfig(_native.FAMILY_STREAM, 256, 128, 64, 4, 4, 8, 0),
+    "pair": _native.GemmConfig(_native.FAMILY_PAIR, 256, 256, 64, 4, 6, 8, 0),
 }
 
 
@@ -198,6 +223,7 @@ def test_full_size_grid_shapes(workload: Workload) -> None:
         ActionCandidate(KernelConfig(64, 64, 64, 4, 2)),
         *[c for c in ALL_CANDIDATES if c.family in ("persistent", "split_k")][:3],
         ActionCandidate(StreamConfig(32, 128, 64, 4, 8, 0)),
+        ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8)),
     ],
     ids=lambda c: c.key,
 )
