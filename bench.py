@@ -336,7 +336,13 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
         }
 
     roofline = family_roofline(dominant)
-    roofline["kernel"] = {"tile": "tile_gemm_kernel", "persistent": "tile_gemm_kernel (persistent grid)", "split_k": "stream_gemm_kernel + splitk_reduce_kernel", "stream": "stream_gemm_kernel"}[dominant]
+    roofline["kernel"] = {
+        "tile": "tile_gemm_kernel",
+        "persistent": "tile_gemm_kernel (persistent grid)",
+        "split_k": "stream_gemm_kernel + splitk_reduce_kernel",
+        "stream": "stream_gemm_kernel",
+        "pair": "pair_gemm_kernel (cta_group::2)",
+    }[dominant]
     roofline.update(_traffic_from_profiles(dominant))
 
     # per-shape roofline fraction (slower of tensor and HBM bound)
@@ -522,7 +528,7 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
             "unit": "TFLOP/s",
             "frac": round(gemm_tflops / peaks["bf16_tflops_sustained"], 4),
             "peak_source": f"{source} (sustained)",
-            "kernel": "tile_gemm_kernel<128,1,256,64> (GEMM phase, per GPU)",
+            "kernel": "pair_gemm_kernel<256,64> (GEMM phase, per GPU)",
             "traffic": None,
         },
         "step_roofline_frac": round(t_roof / (step_ms / 1e3), 4),

@@ -256,8 +256,8 @@ PAIR_M_MINIMUM = 129
 PAIR_CANDIDATES: tuple[ActionCandidate, ...] = _sorted(
     (
         ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8)),
-        ActionCandidate(PairConfig(256, 128, 64, 4, 8, 8)),
         ActionCandidate(PairConfig(256, 256, 64, 4, 6, 16)),
+        ActionCandidate(PairConfig(256, 256, 64, 4, 6, 4)),
     )
 )
 

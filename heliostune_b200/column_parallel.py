@@ -17,11 +17,10 @@ import torch
 import torch.distributed as dist
 
 from heliostune_b200 import _native
-from heliostune_b200.action_configs import ActionCandidate
-from heliostune_b200.configs import KernelConfig
+from heliostune_b200.action_configs import ActionCandidate, PairConfig
 
-#: The GEMM configuration each rank uses for its slice (large M, wide N).
-COLUMN_PARALLEL_CANDIDATE = ActionCandidate(KernelConfig(128, 256, 64, 8, 4))
+#: The GEMM configuration each rank uses for its slice (large M, wide N): CTA-pair 256x256.
+COLUMN_PARALLEL_CANDIDATE = ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8))
 
 
 @dataclass(frozen=True)
