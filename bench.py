@@ -171,9 +171,7 @@ def _launch_count(candidate, workload, sm_count: int) -> int:
     if isinstance(config, SplitKConfig):
         bk = 64 if config.block_k <= 64 else 128
         return 1 + (split_plan(workload.k, bk, config.split_k)[1] > 1)
-    if isinstance(config, StreamConfig):
-        return 1 + (stream_splits(workload.m, workload.n, workload.k, config, sm_count) > 1)
-    return 1
+    return 1  # tile, persistent, pair and stream (in-cluster reduction) are one launch
 
 
 def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
@@ -340,7 +338,7 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
         "tile": "tile_gemm_kernel",
         "persistent": "tile_gemm_kernel (persistent grid)",
         "split_k": "stream_gemm_kernel + splitk_reduce_kernel",
-        "stream": "stream_gemm_kernel",
+        "stream": "stream_cluster_kernel (in-cluster split-K)",
         "pair": "pair_gemm_kernel (cta_group::2)",
     }[dominant]
     roofline.update(_traffic_from_profiles(dominant))

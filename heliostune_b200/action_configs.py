@@ -78,11 +78,12 @@ class SplitKConfig:
 class StreamConfig:
     """B200 weight-streaming GEMM for ``1 <= M <= 256`` (no reference counterpart).
 
-    The CTA owns ``block_n`` (=128, the UMMA M) columns of C and all M rows (padded to a multiple
-    of 16 for the UMMA N). ``block_k`` and ``num_stages`` shape the TMA ring. ``split_k`` = 0 asks
-    the launcher to choose the split so that ``ceil(N/128) * split`` CTAs fill the SMs; a positive
-    value is used as given. One split writes C directly; more write FP32 partials that a second
-    kernel sums in split order.
+    A CTA owns ``block_n`` columns of C (128, or 256 as two UMMA atoms sharing the A tile, for
+    ``block_m`` 64 or 128) and all M rows, padded to ``block_m`` (a power of two >= 16, the UMMA
+    N of the swapped MMA). ``block_k`` and ``num_stages`` shape the TMA ring. ``split_k`` CTAs
+    (1, 2, 4 or 8; 0 asks for the largest that keeps one wave of CTAs on the SMs) divide K and form
+    a thread-block cluster that sums their FP32 partials in split order through distributed
+    shared memory, so no workspace and no second kernel are needed.
     """
 
     block_m: int
@@ -101,10 +102,14 @@ class StreamConfig:
                 raise SchemaError(f"{name} must be a power of two")
         if not 16 <= self.block_m <= STREAM_M_LIMIT:
             raise SchemaError(f"block_m must be between 16 and {STREAM_M_LIMIT}")
-        if self.block_n != 128:
-            raise SchemaError("block_n must be 128 (the UMMA M of the swapped MMA)")
+        if self.block_n not in (128, 256):
+            raise SchemaError("block_n must be 128 or 256")
+        if self.block_n == 256 and self.block_m not in (64, 128):
+            raise SchemaError("block_n 256 needs block_m 64 or 128")
         if self.block_k not in (64, 128):
             raise SchemaError("block_k must be 64 or 128")
+        if self.split_k not in (0, 1, 2, 4, 8):
+            raise SchemaError("split_k must be 0 (automatic), 1, 2, 4 or 8")
         if self.num_warps not in (1, 2, 4, 8):
             raise SchemaError("num_warps must be one of 1, 2, 4, or 8")
 
@@ -298,15 +303,18 @@ STREAM_SMEM_OVERHEAD = 2048
 
 
 def stream_smem_bytes(block_m: int, block_n: int, block_k: int, stages: int) -> int:
-    """Dynamic shared memory of one streaming CTA: the ring of B^T and A^T tiles."""
-    return stages * (block_n + block_m) * block_k * 2 + STREAM_SMEM_OVERHEAD
+    """Dynamic shared memory of one streaming CTA: the TMA ring, reused after the main loop for
+    the FP32 partial the cluster reduction reads."""
+    ring = stages * (block_n + block_m) * block_k * 2
+    partial = block_n * block_m * 4
+    return max(ring, partial) + STREAM_SMEM_OVERHEAD
 
 
 def stream_ctas_per_sm(block_m: int, block_n: int, block_k: int, stages: int) -> int:
     per_cta = stream_smem_bytes(block_m, block_n, block_k, stages) + SMEM_RESERVED_PER_CTA
     by_smem = SMEM_PER_SM // per_cta
-    tmem_columns = max(32, block_m)
-    by_tmem = 512 // tmem_columns
+    columns = (block_n // 128) * block_m
+    by_tmem = 512 // max(32, columns)
     return max(1, min(by_smem, by_tmem, 4))
 
 
@@ -323,12 +331,21 @@ def split_plan(k: int, block_k: int, splits: int) -> tuple[int, int]:
 
 
 def stream_splits(m: int, n: int, k: int, config: StreamConfig, sm_count: int) -> int:
-    """The split factor a :class:`StreamConfig` launches with on a GPU with ``sm_count`` SMs."""
-    if config.split_k:
-        return split_plan(k, config.block_k, config.split_k)[1]
-    n_tiles = -(-n // config.block_n)
-    slots = sm_count * stream_ctas_per_sm(
-        config.block_m, config.block_n, config.block_k, config.num_stages
-    )
-    wanted = max(1, slots // n_tiles)
-    return split_plan(k, config.block_k, wanted)[1]
+    """The cluster size (K splits) a :class:`StreamConfig` launches with on ``sm_count`` SMs.
+
+    Automatic: the largest power of two <= 8 whose CTAs fit one wave. Then, as the launcher does,
+    halve until every split owns K blocks and all but the last the same number.
+    """
+    k_blocks = -(-k // config.block_k)
+    splits = config.split_k
+    if splits == 0:
+        n_tiles = -(-n // config.block_n)
+        slots = sm_count * stream_ctas_per_sm(
+            config.block_m, config.block_n, config.block_k, config.num_stages
+        )
+        splits = 8
+        while splits > 1 and n_tiles * splits > slots:
+            splits //= 2
+    while splits > 1 and (splits > k_blocks or -(-k_blocks // -(-k_blocks // splits)) != splits):
+        splits //= 2
+    return splits

@@ -102,6 +102,7 @@ def _stream_matmul(a: torch.Tensor, b: torch.Tensor, config: StreamConfig) -> to
         _native.check(
             _native.library().hst_matmul_stream(
                 config.block_m,
+                config.block_n,
                 config.block_k,
                 config.num_stages,
                 config.split_k,

@@ -13,6 +13,7 @@
 #include "../../include/heliostune_b200.h"
 #include "gemm_pair.cuh"
 #include "gemm_stream.cuh"
+#include "gemm_stream_cluster.cuh"
 #include "gemm_tile.cuh"
 #include "rmsnorm.cuh"
 
@@ -282,6 +283,18 @@ int stream_ctas_per_sm(int mp, int nt, int bk, int stages) {
   return c < 1 ? 1 : c;
 }
 
+int stream_cluster_ctas_per_sm(int mp, int nt, int bk, int stages) {
+  const int ring = stages * (nt + mp) * bk * 2;
+  const int partial = nt * mp * 4;
+  const int smem = (ring > partial ? ring : partial) + 2048;
+  const int by_smem = kSmemPerSm / (smem + kSmemReservedPerCta);
+  const int cols = (nt / 128) * mp;
+  const int by_tmem = 512 / (cols <= 32 ? 32 : cols);
+  int c = by_smem < by_tmem ? by_smem : by_tmem;
+  if (c > 4) c = 4;
+  return c < 1 ? 1 : c;
+}
+
 int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t m, int64_t n,
               int64_t k, int sms, Plan* p) {
   if (cfg == nullptr) return fail(HST_ERR_INVALID, "configuration is null");
@@ -348,21 +361,30 @@ int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t 
       if (bm < 16 || bm > 256 || bm < m)
         return fail(HST_ERR_INVALID, "stream block_m %d must cover M=%lld (16..256)", bm,
                     static_cast<long long>(m));
-      if (bn != 128) return fail(HST_ERR_UNSUPPORTED, "stream block_n must be 128");
+      if (bn != 128 && bn != 256) return fail(HST_ERR_UNSUPPORTED, "stream block_n must be 128 or 256");
+      if (bn == 256 && (bm < 64 || bm > 128))
+        return fail(HST_ERR_UNSUPPORTED, "stream block_n 256 needs block_m 64 or 128");
       if (bk != 64 && bk != 128) return fail(HST_ERR_UNSUPPORTED, "stream block_k must be 64 or 128");
-      if (cfg->split_k < 0) return fail(HST_ERR_INVALID, "split_k must be >= 0");
-      p->nt = 128;
+      if (cfg->split_k < 0 || cfg->split_k > 8 || (cfg->split_k & (cfg->split_k - 1)))
+        return fail(HST_ERR_INVALID, "stream split_k must be 0 (automatic), 1, 2, 4 or 8");
+      p->nt = bn;
       p->mp = bm;
       p->bk = bk;
       p->stages = cfg->num_stages < 2 ? 2 : (cfg->num_stages > kStreamMaxStages ? kStreamMaxStages : cfg->num_stages);
-      int requested = cfg->split_k;
-      if (requested == 0) {
-        const int64_t n_tiles = cdiv(n, 128);
-        const int64_t slots = int64_t(sms) * stream_ctas_per_sm(p->mp, p->nt, p->bk, p->stages);
-        const int64_t want = slots / n_tiles;
-        requested = static_cast<int>(want < 1 ? 1 : want);
+      const int64_t k_blocks = cdiv(k, bk);
+      int splits = cfg->split_k;
+      if (splits == 0) {
+        // Largest power of two <= 8 whose CTAs still fit one wave of the SMs.
+        const int64_t n_tiles = cdiv(n, bn);
+        const int64_t slots = int64_t(sms) * stream_cluster_ctas_per_sm(p->mp, p->nt, p->bk, p->stages);
+        splits = 8;
+        while (splits > 1 && n_tiles * splits > slots) splits /= 2;
       }
-      split_plan(k, p->bk, requested, &p->kb_per_split, &p->splits);
+      // Every split must own at least one K block and all splits the same count but the last.
+      while (splits > 1 && (splits > k_blocks || cdiv(k_blocks, cdiv(k_blocks, splits)) != splits))
+        splits /= 2;
+      p->splits = splits;
+      p->kb_per_split = static_cast<int>(cdiv(k_blocks, splits));
       break;
     }
     default:
@@ -384,7 +406,8 @@ int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t 
   p->off_c = off;
   if (p->c_tmp) off = align_up(off + size_t(m) * p->ldc_p * 2);
   p->off_p = off;
-  if (is_stream && p->splits > 1) off = align_up(off + size_t(p->splits) * m * n * 4);
+  if (p->family == HST_FAMILY_SPLIT_K && p->splits > 1)
+    off = align_up(off + size_t(p->splits) * m * n * 4);
   p->total = off;
   return HST_OK;
 }
@@ -592,6 +615,69 @@ int dispatch_stream(const DeviceState& dev, const Plan& p, const Operands& o, fl
               p.bk);
 }
 
+template <int NA, int MP, int BK>
+int launch_stream_cluster(const DeviceState& dev, const Operands& o, int stages, int splits,
+                          int kb_per_split, cudaStream_t stream) {
+  using S = ClusterStreamShape<NA, MP, BK>;
+  static std::atomic<uint64_t> smem_done{0};
+  HST_TRY(allow_smem(stream_cluster_kernel<NA, MP, BK>, smem_done));
+  while (stages > 2 && S::smem_bytes(stages) > kMaxDynamicSmem) --stages;
+  if (S::smem_bytes(stages) > kMaxDynamicSmem)
+    return fail(HST_ERR_UNSUPPORTED, "stream tile does not fit shared memory");
+  CUtensorMap ma_, mb_;
+  HST_TRY(encode_tiled_2d(&ma_, o.a, o.k, o.m, o.lda, 64, MP));
+  HST_TRY(encode_tiled_2d(&mb_, o.b, o.n, o.k, o.ldb, 64, BK));
+  ClusterStreamArgs args;
+  args.m = o.m;
+  args.n = o.n;
+  args.k = o.k;
+  args.k_blocks = static_cast<int>(cdiv(o.k, BK));
+  args.kb_per_split = kb_per_split;
+  args.splits = splits;
+  args.stages = stages;
+  args.status = dev.status;
+  args.c = o.c;
+  args.ldc = o.ldc;
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(static_cast<unsigned>(cdiv(o.n, S::kNT)), static_cast<unsigned>(splits));
+  lc.blockDim = dim3(kStreamThreads);
+  lc.dynamicSmemBytes = smem_for_tmem(S::smem_bytes(stages), S::kTmemCols);
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = static_cast<unsigned>(splits);
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = splits > 1 ? 1 : 0;
+  HST_CUDA(cudaLaunchKernelEx(&lc, stream_cluster_kernel<NA, MP, BK>, ma_, mb_, args));
+  return HST_OK;
+}
+
+int dispatch_stream_cluster(const DeviceState& dev, const Plan& p, const Operands& o,
+                            cudaStream_t stream) {
+#define HST_CLUSTER_CASE(NA_, MP_, BK_)                                                   \
+  if (p.nt == 128 * NA_ && p.mp == MP_ && p.bk == BK_)                                    \
+    return launch_stream_cluster<NA_, MP_, BK_>(dev, o, p.stages, p.splits, p.kb_per_split, \
+                                                stream);
+  HST_CLUSTER_CASE(1, 16, 64)
+  HST_CLUSTER_CASE(1, 32, 64)
+  HST_CLUSTER_CASE(1, 64, 64)
+  HST_CLUSTER_CASE(1, 128, 64)
+  HST_CLUSTER_CASE(1, 256, 64)
+  HST_CLUSTER_CASE(1, 16, 128)
+  HST_CLUSTER_CASE(1, 32, 128)
+  HST_CLUSTER_CASE(1, 64, 128)
+  HST_CLUSTER_CASE(1, 128, 128)
+  HST_CLUSTER_CASE(1, 256, 128)
+  HST_CLUSTER_CASE(2, 64, 64)
+  HST_CLUSTER_CASE(2, 128, 64)
+  HST_CLUSTER_CASE(2, 64, 128)
+  HST_CLUSTER_CASE(2, 128, 128)
+#undef HST_CLUSTER_CASE
+  return fail(HST_ERR_UNSUPPORTED, "no stream kernel for %d columns, M %d, K %d", p.nt, p.mp, p.bk);
+}
+
 // ------------------------------------------------------------------------------------------
 // Common GEMM driver
 // ------------------------------------------------------------------------------------------
@@ -661,11 +747,16 @@ int gemm_impl(const hst_gemm_config* cfg, const void* a, int64_t sa0, int64_t sa
     o.ldb = tma_row_stride(vb);
   }
 
-  if (p.family == HST_FAMILY_SPLIT_K || p.family == HST_FAMILY_STREAM) {
+  if (p.family == HST_FAMILY_SPLIT_K) {
     o.c = cc;
     o.ldc = ldc;
     float* partials = reinterpret_cast<float*>(ws + p.off_p);
     return dispatch_stream(*dev, p, o, partials, stream);
+  }
+  if (p.family == HST_FAMILY_STREAM) {
+    o.c = cc;
+    o.ldc = ldc;
+    return dispatch_stream_cluster(*dev, p, o, stream);
   }
 
   // Tile and persistent kernels store C with TMA: 16-byte aligned rows, else a padded copy.
@@ -775,12 +866,12 @@ int hst_matmul_split_k(int32_t block_m, int32_t block_n, int32_t block_k, int32_
                    workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
-int hst_matmul_stream(int32_t block_m, int32_t block_k, int32_t num_stages, int32_t split_k,
-                      const void* a, int64_t a_stride0, int64_t a_stride1, const void* b,
+int hst_matmul_stream(int32_t block_m, int32_t block_n, int32_t block_k, int32_t num_stages,
+                      int32_t split_k, const void* a, int64_t a_stride0, int64_t a_stride1, const void* b,
                       int64_t b_stride0, int64_t b_stride1, void* c, int64_t ldc, int64_t m,
                       int64_t n, int64_t k, void* workspace, size_t workspace_bytes,
                       void* stream) {
-  const hst_gemm_config cfg{HST_FAMILY_STREAM, block_m, 128, block_k, 4, num_stages, 8, split_k};
+  const hst_gemm_config cfg{HST_FAMILY_STREAM, block_m, block_n, block_k, 4, num_stages, 8, split_k};
   return gemm_impl(&cfg, a, a_stride0, a_stride1, b, b_stride0, b_stride1, c, ldc, m, n, k,
                    workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }

@@ -263,6 +263,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   tc_fence_before_sync();
   cluster_sync();  // the leader's UMMAs read the peer's shared memory until here
   if (warp == 1) {
+    __syncwarp();
     tc_fence_after_sync();
     tmem_dealloc_pair(tmem_base, S::kTmemCols);
   }

@@ -1,0 +1,278 @@
+// Weight-streaming GEMM with an in-cluster split-K reduction (the B200 "stream" family).
+//
+// Same swapped MMA as stream_gemm_kernel (C^T tile = B^T * A^T, UMMA M = 128 columns of C,
+// UMMA N = MP rows of A), with two changes for small M:
+//   * a CTA may own NA = 2 column atoms (256 columns of C): both UMMAs share the A^T tile of a
+//     stage, halving the A bytes each CTA pulls per byte of B;
+//   * the S CTAs that split one column tile's K range form a thread-block cluster (1, S, 1).
+//     After the main loop every CTA parks its FP32 accumulator in its own shared memory; after a
+//     cluster barrier CTA r sums columns [r*NT/S, (r+1)*NT/S) of all S partials through
+//     distributed shared memory in split order 0..S-1 and writes FP16 C. No workspace, no second
+//     kernel, no atomics; the result is bitwise reproducible.
+// With S = 1 the epilogue writes C straight from TMEM.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace hst {
+
+struct ClusterStreamArgs {
+  int m, n, k;
+  int k_blocks;
+  int kb_per_split;
+  int splits;  // cluster size along y
+  int stages;
+  int* status;
+  __half* c;
+  int64_t ldc;
+};
+
+template <int NA, int MP, int BK>
+struct ClusterStreamShape {
+  static_assert(NA == 1 || NA == 2, "one or two 128-column atoms per CTA");
+  static_assert(MP % 16 == 0 && MP >= 16 && MP <= 256, "MP must be a multiple of 16 up to 256");
+  static_assert(BK == 64 || BK == 128, "BK must be 64 or 128");
+  static constexpr int kNT = 128 * NA;
+  static constexpr int kAtomsN = kNT / 64;
+  static constexpr int kAtomsK = BK / 64;
+  static constexpr int kWBoxBytes = BK * 128;
+  static constexpr int kXBoxBytes = MP * 128;
+  static constexpr int kWBytes = kAtomsN * kWBoxBytes;
+  static constexpr int kXBytes = kAtomsK * kXBoxBytes;
+  static constexpr int kStageBytes = kWBytes + kXBytes;
+  static constexpr int kPartialBytes = kNT * MP * 4;
+  static constexpr int kCols = NA * MP;
+  static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128 : kCols <= 256 ? 256 : 512;
+  static constexpr uint32_t kIdesc = umma_idesc_f16(128, MP, true, false);
+  static constexpr int kBarrierBytes = 256 + 16 * kStreamMaxStages;
+  static constexpr int smem_bytes(int stages) {
+    const int ring = stages * kStageBytes;
+    return 1024 + (ring > kPartialBytes ? ring : kPartialBytes) + kBarrierBytes;
+  }
+};
+
+template <int NA, int MP, int BK>
+__global__ void __launch_bounds__(kStreamThreads, 1)
+    stream_cluster_kernel(const __grid_constant__ CUtensorMap map_a,
+                          const __grid_constant__ CUtensorMap map_b, const ClusterStreamArgs args) {
+  using S = ClusterStreamShape<NA, MP, BK>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int stages = args.stages;
+  uint8_t* ring = smem;  // after the main loop it holds this CTA's FP32 partial [MP][NT]
+  const int ring_bytes = stages * S::kStageBytes > S::kPartialBytes ? stages * S::kStageBytes
+                                                                     : S::kPartialBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + ring_bytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kStreamMaxStages;
+  uint64_t* tmem_full = bars + 2 * kStreamMaxStages;
+  uint64_t* mma_done = tmem_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* partial = reinterpret_cast<float*>(ring);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = lane_id();
+  const int n0 = blockIdx.x * S::kNT;
+  const int split = blockIdx.y;
+  const int kb_begin = split * args.kb_per_split;
+  const int kb_end = min(kb_begin + args.kb_per_split, args.k_blocks);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tmem_full, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    tma_prefetch_map(&map_a);
+    tma_prefetch_map(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, S::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+  bool have_result = false;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    const uint64_t stream_policy = l2_policy_evict_first();
+    const uint64_t keep_policy = l2_policy_evict_last();
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued_mask = 0, issued_parity = 0;
+    bool ok = true;
+    for (int kb = kb_begin; kb < kb_end; ++kb) {
+      if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+        raise_abort(args.status, abort_flag, kStatusProducerTimeout);
+        ok = false;
+        break;
+      }
+      uint8_t* st = ring + stage * S::kStageBytes;
+      mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+      const int k0 = kb * BK;
+#pragma unroll
+      for (int na = 0; na < S::kAtomsN; ++na) {
+        tma_load_2d(st + na * S::kWBoxBytes, &map_b, &full[stage], n0 + 64 * na, k0, stream_policy);
+      }
+#pragma unroll
+      for (int ka = 0; ka < S::kAtomsK; ++ka) {
+        tma_load_2d(st + S::kWBytes + ka * S::kXBoxBytes, &map_a, &full[stage], k0 + 64 * ka, 0,
+                    keep_policy);
+      }
+      issued_mask |= 1u << stage;
+      issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+      if (++stage == stages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+    if (!ok) {
+      for (int s = 0; s < stages; ++s) {
+        if ((issued_mask & (1u << s)) &&
+            !mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr, 200000000ull)) {
+          atomicOr(args.status, kStatusDrainTimeout);
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- UMMA issuer ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int kb = kb_begin; kb < kb_end; ++kb) {
+      if (!mbar_wait(&full[stage], phase, abort_flag)) {
+        raise_abort(args.status, abort_flag, kStatusMmaTimeout);
+        ok = false;
+        break;
+      }
+      tc_fence_after_sync();
+      const uint32_t w_base = smem_addr(ring + stage * S::kStageBytes);
+      const uint32_t x_base = w_base + S::kWBytes;
+#pragma unroll
+      for (int kk = 0; kk < BK / 16; ++kk) {
+        const uint64_t bdesc =
+            smem_desc(x_base + (kk >> 2) * S::kXBoxBytes + (kk & 3) * 32, 16, 1024);
+#pragma unroll
+        for (int a = 0; a < NA; ++a) {
+          const uint64_t adesc =
+              smem_desc(w_base + a * 2 * S::kWBoxBytes + kk * 2048, S::kWBoxBytes, 1024);
+          umma_f16(tmem_base + a * MP, adesc, bdesc, S::kIdesc,
+                   (kb != kb_begin || kk != 0) ? 1u : 0u);
+        }
+      }
+      umma_commit(&empty[stage]);
+      if (++stage == stages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+    if (ok) umma_commit(tmem_full);
+    umma_commit(mma_done);
+    if (!mbar_wait(mma_done, 0, nullptr, 200000000ull)) atomicOr(args.status, kStatusDrainTimeout);
+  } else if (warp >= 2) {
+    // ---------------- epilogue: TMEM -> C (one split) or -> own shared memory ----------------
+    const int quarter = warp & 3;
+    const bool ready = __all_sync(0xffffffffu, mbar_wait(tmem_full, 0, abort_flag));
+    if (!ready) {
+      if (lane == 0) raise_abort(args.status, abort_flag, kStatusEpilogueTimeout);
+    } else {
+      tc_fence_after_sync();
+      have_result = true;
+      constexpr int kChunk = MP >= 32 ? 32 : 16;
+#pragma unroll 1
+      for (int a = 0; a < NA; ++a) {
+        const int nl = a * 128 + quarter * 32 + static_cast<int>(lane);
+        const int n = n0 + nl;
+        const uint32_t lane_addr =
+            tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * MP;
+#pragma unroll 1
+        for (int c0 = 0; c0 < MP; c0 += kChunk) {
+          if (c0 >= args.m) break;  // warp-uniform
+          float v[kChunk];
+          if constexpr (kChunk == 32) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(lane_addr + c0, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          } else {
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(lane_addr + c0, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+          }
+          if (args.splits == 1) {
+            if (n < args.n) {
+#pragma unroll
+              for (int j = 0; j < kChunk; ++j) {
+                const int m = c0 + j;
+                if (m < args.m) args.c[static_cast<int64_t>(m) * args.ldc + n] = __float2half_rn(v[j]);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) partial[(c0 + j) * S::kNT + nl] = v[j];
+          }
+        }
+      }
+    }
+  }
+
+  if (args.splits > 1) {
+    // ---------------- in-cluster reduction over the S splits ----------------
+    cluster_sync();  // every CTA's partial is in its shared memory
+    const int rank = static_cast<int>(cluster_ctarank());
+    const int cols = S::kNT / args.splits;  // columns this CTA reduces
+    const int quads = cols / 4;
+    const int items = args.m * quads;
+    const uint32_t base = smem_addr(partial);
+    const bool vec_store = (args.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(args.c) & 7) == 0);
+    for (int i = threadIdx.x; i < items; i += blockDim.x) {
+      const int m = i / quads;
+      const int nl = rank * cols + (i % quads) * 4;
+      const uint32_t offset = static_cast<uint32_t>((m * S::kNT + nl) * 4);
+      float4 acc = ld_dsmem_f32x4(map_to_rank(base + offset, 0));
+      for (int s = 1; s < args.splits; ++s) {
+        const float4 v = ld_dsmem_f32x4(map_to_rank(base + offset, static_cast<uint32_t>(s)));
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      const int n = n0 + nl;
+      __half* dst = args.c + static_cast<int64_t>(m) * args.ldc + n;
+      if (vec_store && n + 3 < args.n) {
+        __half2 lo = __floats2half2_rn(acc.x, acc.y);
+        __half2 hi = __floats2half2_rn(acc.z, acc.w);
+        uint2 packed;
+        packed.x = *reinterpret_cast<uint32_t*>(&lo);
+        packed.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(dst) = packed;
+      } else {
+        const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+        for (int j = 0; j < 4 && n + j < args.n; ++j) dst[j] = __float2half_rn(vals[j]);
+      }
+    }
+    cluster_sync();  // peers finished reading this CTA's shared memory
+  }
+  (void)have_result;
+
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, S::kTmemCols);
+  }
+}
+
+}  // namespace hst

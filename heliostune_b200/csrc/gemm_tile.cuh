@@ -286,6 +286,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   tc_fence_before_sync();
   __syncthreads();
   if (warp == 1) {
+    __syncwarp();
     tc_fence_after_sync();
     tmem_dealloc(tmem_base, S::kTmemCols);
   }

@@ -267,8 +267,21 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
   return r;
 }
 
-// Whole-cluster execution barrier (all threads of both CTAs).
+// Four FP32 values from (possibly another CTA's) shared memory at a shared::cluster address.
+__device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
+
+// Whole-cluster execution barrier (all threads of all CTAs of the cluster). The warp is
+// reconverged first: the .aligned barrier needs every lane at the same instruction, and callers
+// reach it from role branches that only lane 0 of a warp entered.
 __device__ __forceinline__ void cluster_sync() {
+  __syncwarp();
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
                    : "memory");
 }

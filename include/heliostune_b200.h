@@ -101,9 +101,12 @@ int hst_matmul_split_k(int32_t block_m, int32_t block_n, int32_t block_k, int32_
                        void* c, int64_t ldc, int64_t m, int64_t n, int64_t k, void* workspace,
                        size_t workspace_bytes, void* stream);
 
-/* B200 weight-streaming family (no reference counterpart): 1 <= m <= 256; split_k = 0 chooses
- * the split that fills the SMs. */
-int hst_matmul_stream(int32_t block_m, int32_t block_k, int32_t num_stages, int32_t split_k,
+/* B200 weight-streaming family (no reference counterpart): 1 <= m <= 256, block_n 128 or 256
+ * columns of C per CTA (256 needs block_m 64 or 128). split_k (1, 2, 4 or 8; 0 = the largest that
+ * fills one wave) CTAs form a cluster whose partials are summed in split order through
+ * distributed shared memory: no workspace for aligned operands. */
+int hst_matmul_stream(int32_t block_m, int32_t block_n, int32_t block_k, int32_t num_stages,
+                      int32_t split_k,
                       const void* a, int64_t a_stride0, int64_t a_stride1, const void* b,
                       int64_t b_stride0, int64_t b_stride1, void* c, int64_t ldc, int64_t m,
                       int64_t n, int64_t k, void* workspace, size_t workspace_bytes,

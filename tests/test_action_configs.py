@@ -162,10 +162,18 @@ def test_stream_family() -> None:
     assert set(candidates_for(w)) <= set(b200_candidates_for(w))
     with pytest.raises(SchemaError):
         StreamConfig(16, 64, 64, 4, 8, 0)
-    # The automatic split fills 148 SMs without exceeding one wave of CTAs.
-    config = StreamConfig(16, 128, 64, 4, 8, 0)
-    splits = stream_splits(1, 3584, 18944, config, 148)
-    assert 28 * splits <= 148 and 28 * (splits + 1) > 148
+    with pytest.raises(SchemaError):
+        StreamConfig(16, 256, 64, 4, 8, 0)
+    with pytest.raises(SchemaError):
+        StreamConfig(16, 128, 64, 4, 8, 3)
+    # The automatic split is the largest power of two <= 8 that keeps one wave of CTAs.
+    one_per_sm = StreamConfig(16, 128, 64, 4, 8, 0)  # 146 KB of shared memory
+    assert stream_splits(1, 3584, 18944, one_per_sm, 148) == 4  # 28 tiles x 4 = 112 CTAs
+    two_per_sm = StreamConfig(16, 128, 64, 4, 6, 0)
+    assert stream_splits(1, 3584, 18944, two_per_sm, 148) == 8  # 224 CTAs on 296 slots
+    assert stream_splits(1, 37888, 3584, one_per_sm, 148) == 1  # 296 tiles already fill the GPU
+    # every split owns K blocks: K = 100 is two blocks of 64
+    assert stream_splits(1, 256, 100, StreamConfig(16, 128, 64, 4, 8, 8), 148) == 2
 
 
 def test_split_plan_matches_the_reference_interval_rule() -> None:

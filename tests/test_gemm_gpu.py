@@ -101,8 +101,9 @@ def test_stream_family(m: int) -> None:
     assert candidates
     for candidate in candidates:
         assert_gemm_parity(launch(a, b, candidate), a, b)
-    fixed = ActionCandidate(StreamConfig(stream_block_m(m), 128, 64, 4, 4, 3))
-    assert_gemm_parity(launch(a, b, fixed), a, b)
+    for split in (1, 2, 4, 8):
+        fixed = ActionCandidate(StreamConfig(stream_block_m(m), 128, 64, 4, 4, split))
+        assert_gemm_parity(launch(a, b, fixed), a, b)
 
 
 @pytest.mark.parametrize("candidate", PAIR_CANDIDATES, ids=lambda c: c.key)
@@ -159,6 +160,7 @@ ABI_CONFIGS = {
     "persistent": _native.GemmConfig(_native.FAMILY_PERSISTENT, 128, 256, 64, 8, 3, 8, 0),
     "split_k": _native.GemmConfig(_native.FAMILY_SPLIT_K, 16, 128, 64, 4, 3, 8, 16),
     "stream": _native.GemmConfig(_native.FAMILY_STREAM, 256, 128, 64, 4, 4, 8, 0),
+    "stream2": _native.GemmConfig(_native.FAMILY_STREAM, 128, 256, 64, 4, 3, 8, 4),
     "pair": _native.GemmConfig(_native.FAMILY_PAIR, 256, 256, 64, 4, 6, 8, 0),
 }
 
@@ -169,7 +171,7 @@ def test_golden_fixtures_through_the_c_abi(name: str, family: str) -> None:
     cases = np.load(GOLDEN / "gemm_cases.npz")
     a_np, b_np = cases[f"{name}_a"], cases[f"{name}_b"]
     m = a_np.shape[0]
-    if family == "split_k" and m > 31 or family == "stream" and m > 256:
+    if family == "split_k" and m > 31 or family.startswith("stream") and m > (128 if family == "stream2" else 256):
         pytest.skip("outside the family's M range")
     a = torch.from_numpy(a_np).cuda()
     b = torch.from_numpy(b_np).cuda()
@@ -223,12 +225,14 @@ def test_full_size_grid_shapes(workload: Workload) -> None:
         ActionCandidate(KernelConfig(64, 64, 64, 4, 2)),
         *[c for c in ALL_CANDIDATES if c.family in ("persistent", "split_k")][:3],
         ActionCandidate(StreamConfig(32, 128, 64, 4, 8, 0)),
+        ActionCandidate(StreamConfig(32, 128, 64, 4, 6, 8)),
+        ActionCandidate(StreamConfig(128, 256, 64, 4, 3, 4)),
         ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8)),
     ],
     ids=lambda c: c.key,
 )
 def test_bitwise_reproducible_and_inputs_untouched(candidate: ActionCandidate) -> None:
-    m = 31 if candidate.family in ("split_k", "stream") else 300
+    m = 31 if candidate.family == "split_k" else (100 if candidate.family == "stream" else 300)
     k, n = 4096, 3584
     g = torch.Generator(device="cuda").manual_seed(5)
     a = scaled_normal((m, k), k, g)
