@@ -134,7 +134,7 @@ def _declare(lib: ctypes.CDLL) -> None:
             ctypes.c_int,
         ),
         "hst_matmul_pair": (
-            [_i32] * 4 + [_ptr, _i64, _i64, _ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i64,
+            [_i32] * 5 + [_ptr, _i64, _i64, _ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i64,
                           _ptr, _size, _ptr],
             ctypes.c_int,
         ),

@@ -133,7 +133,9 @@ class PairConfig:
     loads its 128 rows of A and half of the tile's ``block_n`` columns of B, so each SM moves
     half the B bytes of a single-SM tile. Persistent over the tiles in ``group_m`` raster order
     with two TMEM accumulators; ``num_stages`` is the ring depth per CTA. ``num_warps`` is kept
-    for the key (the CTA runs six warps).
+    for the key (the CTA runs six warps). ``split_k`` 2 or 4 (0 = automatic, only when the tiles
+    would leave most SMs idle) lets 2 x ``split_k`` CTAs share one tile and sum their FP32
+    partials in split order through distributed shared memory.
     """
 
     block_m: int
@@ -142,6 +144,7 @@ class PairConfig:
     num_warps: int
     num_stages: int
     group_m: int = 8
+    split_k: int = 1
 
     def __post_init__(self) -> None:
         for name in ("block_m", "block_n", "block_k", "num_warps", "num_stages", "group_m"):
@@ -154,12 +157,16 @@ class PairConfig:
             raise SchemaError("block_k must be 64 or 128")
         if self.num_warps not in (1, 2, 4, 8):
             raise SchemaError("num_warps must be one of 1, 2, 4, or 8")
+        exact_int(self.split_k, context="pair config split_k", minimum=0)
+        if self.split_k not in (0, 1, 2, 4):
+            raise SchemaError("split_k must be 0 (automatic), 1, 2 or 4")
 
     @property
     def key(self) -> str:
+        split = "" if self.split_k == 1 else f"-split{'auto' if self.split_k == 0 else self.split_k}"
         return (
             f"pair-m{self.block_m}n{self.block_n}k{self.block_k}"
-            f"-w{self.num_warps}s{self.num_stages}g{self.group_m}"
+            f"-w{self.num_warps}s{self.num_stages}g{self.group_m}{split}"
         )
 
     def to_dict(self) -> dict[str, int]:
@@ -265,11 +272,24 @@ PAIR_CANDIDATES: tuple[ActionCandidate, ...] = _sorted(
         ActionCandidate(PairConfig(256, 256, 64, 4, 6, 4)),
     )
 )
+#: Split-K pair candidates, offered while a 256 x 256 tiling leaves most SM pairs idle.
+PAIR_SPLIT_CANDIDATES: tuple[ActionCandidate, ...] = _sorted(
+    (
+        ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8, 2)),
+        ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8, 4)),
+        ActionCandidate(PairConfig(256, 128, 64, 4, 8, 8, 2)),
+    )
+)
 
 
 def pair_candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:
     """B200 CTA-pair candidates for ``M > 128`` (empty below)."""
-    return PAIR_CANDIDATES if workload.m >= PAIR_M_MINIMUM else ()
+    if workload.m < PAIR_M_MINIMUM:
+        return ()
+    tiles = -(-workload.m // 256) * -(-workload.n // 256)
+    if tiles <= 40:
+        return _sorted((*PAIR_CANDIDATES, *PAIR_SPLIT_CANDIDATES))
+    return PAIR_CANDIDATES
 
 
 def b200_candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:

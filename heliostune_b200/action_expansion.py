@@ -137,7 +137,7 @@ def _pair_matmul(a: torch.Tensor, b: torch.Tensor, config: PairConfig) -> torch.
         config.num_warps,
         config.num_stages,
         config.group_m,
-        0,
+        config.split_k,
     )
     workspace, ws_ptr, ws_bytes = _workspace(native, a, b, m, n, k)
     with torch.cuda.device(a.device):
@@ -147,6 +147,7 @@ def _pair_matmul(a: torch.Tensor, b: torch.Tensor, config: PairConfig) -> torch.
                 config.block_k,
                 config.num_stages,
                 config.group_m,
+                config.split_k,
                 a.data_ptr(),
                 a.stride(0),
                 a.stride(1),

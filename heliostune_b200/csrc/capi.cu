@@ -333,12 +333,26 @@ int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t 
       if (bm != 256) return fail(HST_ERR_UNSUPPORTED, "pair tiles have block_m 256");
       if (bn != 128 && bn != 256) return fail(HST_ERR_UNSUPPORTED, "pair block_n must be 128 or 256");
       if (bk != 64 && bk != 128) return fail(HST_ERR_UNSUPPORTED, "pair block_k must be 64 or 128");
+      if (cfg->split_k < 0 || cfg->split_k > 4 || cfg->split_k == 3)
+        return fail(HST_ERR_INVALID, "pair split_k must be 0 (automatic), 1, 2 or 4");
       p->um = 128;
       p->ma = 2;
       p->bn = bn;
       p->bk = bk;
       p->stages = cfg->num_stages < 2 ? 2 : (cfg->num_stages > kMaxStages ? kMaxStages : cfg->num_stages);
       p->group_m = cfg->group_m;
+      const int64_t tiles = cdiv(m, 256) * cdiv(n, bn);
+      const int64_t k_blocks = cdiv(k, bk);
+      int splits = cfg->split_k;
+      if (splits == 0) {
+        // Split K only while the tiles leave half the SM pairs idle.
+        splits = 1;
+        while (splits < 4 && tiles * splits * 2 <= sms / 2) splits *= 2;
+      }
+      while (splits > 1 && (splits > k_blocks || cdiv(k_blocks, cdiv(k_blocks, splits)) != splits))
+        splits /= 2;
+      p->splits = splits;
+      p->kb_per_split = static_cast<int>(cdiv(k_blocks, splits));
       break;
     }
     case HST_FAMILY_SPLIT_K: {
@@ -491,13 +505,17 @@ int dispatch_tile(const DeviceState& dev, const Plan& p, const Operands& o, bool
 // CTA-pair launch
 // ------------------------------------------------------------------------------------------
 
-template <int BN, int BK>
-int launch_pair(const DeviceState& dev, const Operands& o, int stages, int group_m,
-                cudaStream_t stream) {
+template <int BN, int BK, bool SPLIT>
+int launch_pair(const DeviceState& dev, const Operands& o, int stages, int group_m, int splits,
+                int kb_per_split, cudaStream_t stream) {
   using S = PairShape<BN, BK>;
   static std::atomic<uint64_t> smem_done{0};
-  HST_TRY(allow_smem(pair_gemm_kernel<BN, BK>, smem_done));
+  HST_TRY(allow_smem(pair_gemm_kernel<BN, BK, SPLIT>, smem_done));
   while (stages > 2 && S::smem_bytes(stages) > kMaxDynamicSmem) --stages;
+  if (SPLIT) {
+    // The parked FP32 partial (128 x BN) reuses the drained ring.
+    while (stages * S::kStageBytes < 128 * BN * 4) ++stages;
+  }
   if (S::smem_bytes(stages) > kMaxDynamicSmem)
     return fail(HST_ERR_UNSUPPORTED, "pair tile 256x%dx%d does not fit shared memory", BN, BK);
   CUtensorMap ma_, mb_, mc_;
@@ -515,29 +533,43 @@ int launch_pair(const DeviceState& dev, const Operands& o, int stages, int group
   args.group_m = group_m;
   args.stages = stages;
   args.status = dev.status;
+  PairSplitArgs split_args;
+  split_args.splits = splits;
+  split_args.kb_per_split = kb_per_split;
+  split_args.c = o.c;
+  split_args.ldc = o.ldc;
   const int max_pairs = dev.sm_count / 2;
   const int pairs = args.num_tiles < max_pairs ? args.num_tiles : max_pairs;
   cudaLaunchConfig_t lc = {};
-  lc.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  lc.gridDim = SPLIT ? dim3(static_cast<unsigned>(2 * args.num_tiles), static_cast<unsigned>(splits))
+                     : dim3(static_cast<unsigned>(2 * pairs));
   lc.blockDim = dim3(kTileThreads);
   lc.dynamicSmemBytes = S::smem_bytes(stages);
   lc.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.y = SPLIT ? static_cast<unsigned>(splits) : 1;
   attr[0].val.clusterDim.z = 1;
   lc.attrs = attr;
   lc.numAttrs = 1;
-  HST_CUDA(cudaLaunchKernelEx(&lc, pair_gemm_kernel<BN, BK>, ma_, mb_, mc_, args));
+  HST_CUDA(cudaLaunchKernelEx(&lc, pair_gemm_kernel<BN, BK, SPLIT>, ma_, mb_, mc_, args, split_args));
   return HST_OK;
 }
 
 int dispatch_pair(const DeviceState& dev, const Plan& p, const Operands& o, cudaStream_t stream) {
-  if (p.bn == 256 && p.bk == 64) return launch_pair<256, 64>(dev, o, p.stages, p.group_m, stream);
-  if (p.bn == 128 && p.bk == 64) return launch_pair<128, 64>(dev, o, p.stages, p.group_m, stream);
-  if (p.bn == 256 && p.bk == 128) return launch_pair<256, 128>(dev, o, p.stages, p.group_m, stream);
-  if (p.bn == 128 && p.bk == 128) return launch_pair<128, 128>(dev, o, p.stages, p.group_m, stream);
+#define HST_PAIR_CASE(BN_, BK_)                                                                \
+  if (p.bn == BN_ && p.bk == BK_) {                                                            \
+    if (p.splits > 1)                                                                          \
+      return launch_pair<BN_, BK_, true>(dev, o, p.stages, p.group_m, p.splits, p.kb_per_split, \
+                                         stream);                                              \
+    return launch_pair<BN_, BK_, false>(dev, o, p.stages, p.group_m, 1, 0, stream);            \
+  }
+  HST_PAIR_CASE(256, 64)
+  HST_PAIR_CASE(128, 64)
+  HST_PAIR_CASE(256, 128)
+  HST_PAIR_CASE(128, 128)
+#undef HST_PAIR_CASE
   return fail(HST_ERR_UNSUPPORTED, "no pair kernel for N %d, K %d", p.bn, p.bk);
 }
 
@@ -877,10 +909,11 @@ int hst_matmul_stream(int32_t block_m, int32_t block_n, int32_t block_k, int32_t
 }
 
 int hst_matmul_pair(int32_t block_n, int32_t block_k, int32_t num_stages, int32_t group_m,
-                    const void* a, int64_t a_stride0, int64_t a_stride1, const void* b,
+                    int32_t split_k, const void* a, int64_t a_stride0, int64_t a_stride1, const void* b,
                     int64_t b_stride0, int64_t b_stride1, void* c, int64_t ldc, int64_t m,
                     int64_t n, int64_t k, void* workspace, size_t workspace_bytes, void* stream) {
-  const hst_gemm_config cfg{HST_FAMILY_PAIR, 256, block_n, block_k, 4, num_stages, group_m, 0};
+  const hst_gemm_config cfg{HST_FAMILY_PAIR, 256, block_n, block_k, 4, num_stages, group_m,
+                            split_k};
   return gemm_impl(&cfg, a, a_stride0, a_stride1, b, b_stride0, b_stride1, c, ldc, m, n, k,
                    workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }

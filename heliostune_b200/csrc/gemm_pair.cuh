@@ -14,6 +14,13 @@
 //     epilogue warps report a free accumulator on the leader's barrier.
 // The kernel is persistent: cluster p walks tiles p, p + #pairs, ... in the grouped raster, with
 // two TMEM accumulators so a tile's epilogue overlaps the next tile's main loop.
+//
+// SPLIT = true (split-K for tile counts far below the SM count): the cluster grows to (2, S):
+// S pairs compute the same 256 x BN tile over S contiguous K ranges. Each CTA parks its FP32
+// 128 x BN partial in its own shared memory (the drained ring, 16-byte chunks swizzled by row);
+// after a cluster barrier CTA (r, s) sums columns [s*BN/S, (s+1)*BN/S) of its 128 rows over the S
+// partials through distributed shared memory, in split order, and stores FP16 C. One tile per
+// cluster; no workspace, no atomics, bitwise reproducible.
 // No TMA load here feeds more than one CTA's shared memory.
 #pragma once
 
@@ -44,12 +51,21 @@ struct PairShape {
   }
 };
 
-template <int BN, int BK>
+struct PairSplitArgs {
+  int splits;        // cluster extent along y (1 = persistent mode)
+  int kb_per_split;  // K blocks of one split
+  __half* c;         // C for the split-mode epilogue (row stride ldc)
+  int64_t ldc;
+};
+
+template <int BN, int BK, bool SPLIT>
 __global__ void __launch_bounds__(kTileThreads, 1)
     pair_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                      const __grid_constant__ CUtensorMap map_b,
-                     const __grid_constant__ CUtensorMap map_c, const TileArgs args) {
+                     const __grid_constant__ CUtensorMap map_c, const TileArgs args,
+                     const PairSplitArgs split_args) {
   using S = PairShape<BN, BK>;
+  static_assert(!SPLIT || BN * 128 * 4 <= 6 * 32768, "the FP32 partial reuses the ring");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -67,9 +83,14 @@ __global__ void __launch_bounds__(kTileThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = lane_id();
-  const uint32_t rank = cluster_ctarank();
-  const int pair = static_cast<int>(cluster_id_x());
-  const int pairs = static_cast<int>(nclusters_x());
+  const uint32_t crank = cluster_ctarank();
+  const uint32_t rank = crank & 1u;           // row half of the pair tile
+  const uint32_t leader = crank & ~1u;        // cluster rank of this pair's leader CTA
+  const int pair = SPLIT ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(cluster_id_x());
+  const int pairs = SPLIT ? args.num_tiles : static_cast<int>(nclusters_x());
+  const int split = SPLIT ? static_cast<int>(blockIdx.y) : 0;
+  const int kb_begin = SPLIT ? split * split_args.kb_per_split : 0;
+  const int kb_end = SPLIT ? min(kb_begin + split_args.kb_per_split, args.k_blocks) : args.k_blocks;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -108,14 +129,14 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       grouped_tile(tile, args.tiles_m, args.tiles_n, args.group_m, pm, pn);
       const int m0 = pm * 256 + static_cast<int>(rank) * 128;
       const int n0 = pn * BN + static_cast<int>(rank) * S::kHalfN;
-      for (int kb = 0; kb < args.k_blocks; ++kb) {
+      for (int kb = kb_begin; kb < kb_end; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
           raise_abort(args.status, abort_flag, kStatusProducerTimeout);
           ok = false;
           break;
         }
         uint8_t* st = ring + stage * S::kStageBytes;
-        const uint32_t leader_full = map_to_rank(smem_addr(&full[stage]), 0);
+        const uint32_t leader_full = map_to_rank(smem_addr(&full[stage]), leader);
         if (rank == 0) {
           mbar_arrive_expect_tx(&full[stage], 2 * S::kStageBytes);
           armed_mask |= 1u << stage;
@@ -160,7 +181,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       }
       tc_fence_after_sync();
       const uint32_t d_base = tmem_base + acc * S::kAccCols;
-      for (int kb = 0; kb < args.k_blocks; ++kb) {
+      for (int kb = kb_begin; kb < kb_end; ++kb) {
         if (!mbar_wait(&full[stage], phase, abort_flag)) {
           raise_abort(args.status, abort_flag, kStatusMmaTimeout);
           ok = false;
@@ -174,11 +195,11 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           const uint64_t adesc =
               smem_desc(a_base + (kk >> 2) * S::kABoxBytes + (kk & 3) * 32, 16, 1024);
           const uint64_t bdesc = smem_desc(b_base + kk * 2048, S::kBBoxBytes, 1024);
-          umma_f16_pair(d_base, adesc, bdesc, S::kIdesc, (kb | kk) != 0);
+          umma_f16_pair(d_base, adesc, bdesc, S::kIdesc, (kb != kb_begin || kk != 0) ? 1u : 0u);
         }
         const uint32_t own_empty = smem_addr(&empty[stage]);
         umma_commit_pair(own_empty);
-        umma_commit_pair(map_to_rank(own_empty, 1));
+        umma_commit_pair(map_to_rank(own_empty, crank | 1u));
         if (++stage == stages) {
           stage = 0;
           phase ^= 1u;
@@ -187,7 +208,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       if (!ok) break;
       const uint32_t own_full = smem_addr(&tmem_full[acc]);
       umma_commit_pair(own_full);
-      umma_commit_pair(map_to_rank(own_full, 1));
+      umma_commit_pair(map_to_rank(own_full, crank | 1u));
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -195,7 +216,30 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     }
     umma_commit_pair(smem_addr(mma_done));
     if (!mbar_wait(mma_done, 0, nullptr, 200000000ull)) atomicOr(args.status, kStatusDrainTimeout);
-  } else if (warp >= 2) {
+  } else if (SPLIT && warp >= 2) {
+    // ---------------- split mode: park the FP32 partial in shared memory ----------------
+    const int quarter = warp & 3;
+    const bool ready = __all_sync(0xffffffffu, mbar_wait(&tmem_full[0], 0, abort_flag));
+    if (!ready) {
+      if (lane == 0) raise_abort(args.status, abort_flag, kStatusEpilogueTimeout);
+    } else {
+      tc_fence_after_sync();
+      const uint32_t row = static_cast<uint32_t>(quarter * 32) + lane;
+      const uint32_t row_addr = smem_addr(ring) + row * (BN * 4);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + c, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t chunk = static_cast<uint32_t>(c / 4 + j);
+          st_shared_v4(row_addr + ((chunk ^ (row & 7u)) << 4), v[4 * j], v[4 * j + 1],
+                       v[4 * j + 2], v[4 * j + 3]);
+        }
+      }
+    }
+  } else if (!SPLIT && warp >= 2) {
     // ---------------- epilogue (both CTAs, own 128 rows) ----------------
     const int quarter = warp & 3;
     uint8_t* staging = epi + (warp - 2) * 2 * kEpilogueStageBytes;
@@ -248,7 +292,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         if (rank == 0) {
           mbar_arrive(&tmem_empty[acc]);
         } else {
-          mbar_arrive_cluster(map_to_rank(smem_addr(&tmem_empty[acc]), 0));
+          mbar_arrive_cluster(map_to_rank(smem_addr(&tmem_empty[acc]), leader));
         }
       }
       if (++acc == 2) {
@@ -258,6 +302,50 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     }
     if (lane == 0) bulk_wait_group<0>();
     __syncwarp();
+  }
+
+  if constexpr (SPLIT) {
+    // ---------------- split mode: sum the S partials of this row half over DSMEM ----------------
+    cluster_sync();  // every CTA's partial is parked
+    const int splits = split_args.splits;
+    const int cols = BN / splits;      // columns this CTA sums and stores
+    const int chunks = cols / 4;       // 16-byte chunks per row
+    int pm, pn;
+    grouped_tile(pair, args.tiles_m, args.tiles_n, args.group_m, pm, pn);
+    const int row_base = pm * 256 + static_cast<int>(rank) * 128;
+    const int col_base = pn * BN + split * cols;
+    const uint32_t base = smem_addr(ring);
+    const bool vec = (split_args.ldc % 4 == 0) &&
+                     ((reinterpret_cast<uintptr_t>(split_args.c) & 7) == 0);
+    for (int i = threadIdx.x; i < 128 * chunks; i += blockDim.x) {
+      const uint32_t row = static_cast<uint32_t>(i / chunks);
+      const uint32_t chunk = static_cast<uint32_t>(split * chunks + i % chunks);
+      const uint32_t offset = row * (BN * 4) + ((chunk ^ (row & 7u)) << 4);
+      float4 acc = ld_dsmem_f32x4(map_to_rank(base + offset, rank));
+      for (int s2 = 1; s2 < splits; ++s2) {
+        const float4 v = ld_dsmem_f32x4(map_to_rank(base + offset, rank + 2u * s2));
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      const int m = row_base + static_cast<int>(row);
+      const int n = col_base + (i % chunks) * 4;
+      if (m < args.m) {
+        __half* dst = split_args.c + static_cast<int64_t>(m) * split_args.ldc + n;
+        if (vec && n + 3 < args.n) {
+          __half2 lo = __floats2half2_rn(acc.x, acc.y);
+          __half2 hi = __floats2half2_rn(acc.z, acc.w);
+          uint2 packed;
+          packed.x = *reinterpret_cast<uint32_t*>(&lo);
+          packed.y = *reinterpret_cast<uint32_t*>(&hi);
+          *reinterpret_cast<uint2*>(dst) = packed;
+        } else {
+          const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+          for (int j = 0; j < 4 && n + j < args.n; ++j) dst[j] = __float2half_rn(vals[j]);
+        }
+      }
+    }
   }
 
   tc_fence_before_sync();

@@ -112,11 +112,13 @@ int hst_matmul_stream(int32_t block_m, int32_t block_n, int32_t block_k, int32_t
                       int64_t n, int64_t k, void* workspace, size_t workspace_bytes,
                       void* stream);
 
-/* B200 CTA-pair family (no reference counterpart): persistent clusters of two CTAs computing
- * 256 x block_n tiles (block_n 128 or 256) with tcgen05.mma.cta_group::2. Any strides (packed
- * through the workspace when a TMA tensor map cannot describe them). */
+/* B200 CTA-pair family (no reference counterpart): clusters of two CTAs computing 256 x block_n
+ * tiles (block_n 128 or 256) with tcgen05.mma.cta_group::2, persistent over the tiles. split_k
+ * 2 or 4 (0 = automatic when the tiles leave most SMs idle) makes clusters of 2 x split_k CTAs
+ * that divide K and sum their partials in split order through distributed shared memory. Any
+ * strides (packed through the workspace when a TMA tensor map cannot describe them). */
 int hst_matmul_pair(int32_t block_n, int32_t block_k, int32_t num_stages, int32_t group_m,
-                    const void* a, int64_t a_stride0, int64_t a_stride1, const void* b,
+                    int32_t split_k, const void* a, int64_t a_stride0, int64_t a_stride1, const void* b,
                     int64_t b_stride0, int64_t b_stride1, void* c, int64_t ldc, int64_t m,
                     int64_t n, int64_t k, void* workspace, size_t workspace_bytes, void* stream);
 

@@ -120,6 +120,23 @@ def test_pair_family(candidate: ActionCandidate, shape: tuple[int, int, int]) ->
     assert_gemm_parity(launch(a, b, candidate), a, b)
 
 
+@pytest.mark.parametrize("split", (2, 4))
+@pytest.mark.parametrize("block_n", (128, 256))
+@pytest.mark.parametrize(
+    "shape", ((512, 4096, 4096), (300, 1032, 520), (129, 264, 2000), (512, 4608, 3584)),
+    ids=lambda s: "x".join(map(str, s)),
+)
+def test_pair_split_k(split: int, block_n: int, shape: tuple[int, int, int]) -> None:
+    m, n, k = shape
+    g = torch.Generator(device="cuda").manual_seed(m * split + block_n)
+    a = scaled_normal((m, k), k, g)
+    b = scaled_normal((k, n), k, g)
+    candidate = ActionCandidate(PairConfig(256, block_n, 64, 4, 6, 8, split))
+    first = launch(a, b, candidate)
+    assert_gemm_parity(first, a, b)
+    assert torch.equal(first.view(torch.int16), launch(a, b, candidate).view(torch.int16))
+
+
 def test_pair_family_with_strided_operands_and_deep_k() -> None:
     g = torch.Generator(device="cuda").manual_seed(9)
     a = scaled_normal((300, 2 * 1540), 1540, g)[:, ::2]
