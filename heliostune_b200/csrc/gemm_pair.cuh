@@ -16,11 +16,13 @@
 // two TMEM accumulators so a tile's epilogue overlaps the next tile's main loop.
 //
 // SPLIT = true (split-K for tile counts far below the SM count): the cluster grows to (2, S):
-// S pairs compute the same 256 x BN tile over S contiguous K ranges. Each CTA parks its FP32
-// 128 x BN partial in its own shared memory (the drained ring, 16-byte chunks swizzled by row);
-// after a cluster barrier CTA (r, s) sums columns [s*BN/S, (s+1)*BN/S) of its 128 rows over the S
-// partials through distributed shared memory, in split order, and stores FP16 C. One tile per
-// cluster; no workspace, no atomics, bitwise reproducible.
+// S pairs compute the same 256 x BN tile over S contiguous K ranges. CTA (r, s) owns columns
+// [s*BN/S, (s+1)*BN/S) of its 128 rows. Once every CTA's main loop is done (cluster barrier, so
+// all rings are drained), each CTA pushes every column slice of its FP32 partial from TMEM
+// straight into the owning CTA's shared memory (remote stores, slot = source split, 16-byte
+// chunks swizzled by row); after a second barrier each owner sums its S slots in split order
+// from local shared memory and stores FP16 C. One tile per cluster; no workspace, no atomics,
+// bitwise reproducible.
 // No TMA load here feeds more than one CTA's shared memory.
 #pragma once
 
@@ -116,6 +118,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   cluster_sync();  // both CTAs' barriers exist before either signals the other
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  bool split_ready = false;
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer (both CTAs) ----------------
@@ -217,28 +220,9 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     umma_commit_pair(smem_addr(mma_done));
     if (!mbar_wait(mma_done, 0, nullptr, 200000000ull)) atomicOr(args.status, kStatusDrainTimeout);
   } else if (SPLIT && warp >= 2) {
-    // ---------------- split mode: park the FP32 partial in shared memory ----------------
-    const int quarter = warp & 3;
-    const bool ready = __all_sync(0xffffffffu, mbar_wait(&tmem_full[0], 0, abort_flag));
-    if (!ready) {
-      if (lane == 0) raise_abort(args.status, abort_flag, kStatusEpilogueTimeout);
-    } else {
-      tc_fence_after_sync();
-      const uint32_t row = static_cast<uint32_t>(quarter * 32) + lane;
-      const uint32_t row_addr = smem_addr(ring) + row * (BN * 4);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + c, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t chunk = static_cast<uint32_t>(c / 4 + j);
-          st_shared_v4(row_addr + ((chunk ^ (row & 7u)) << 4), v[4 * j], v[4 * j + 1],
-                       v[4 * j + 2], v[4 * j + 3]);
-        }
-      }
-    }
+    // ---------------- split mode: wait for the accumulator; the push follows below ----------
+    split_ready = __all_sync(0xffffffffu, mbar_wait(&tmem_full[0], 0, abort_flag));
+    if (!split_ready && lane == 0) raise_abort(args.status, abort_flag, kStatusEpilogueTimeout);
   } else if (!SPLIT && warp >= 2) {
     // ---------------- epilogue (both CTAs, own 128 rows) ----------------
     const int quarter = warp & 3;
@@ -305,32 +289,57 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   }
 
   if constexpr (SPLIT) {
-    // ---------------- split mode: sum the S partials of this row half over DSMEM ----------------
-    cluster_sync();  // every CTA's partial is parked
     const int splits = split_args.splits;
-    const int cols = BN / splits;      // columns this CTA sums and stores
-    const int chunks = cols / 4;       // 16-byte chunks per row
+    const int cols = BN / splits;              // columns each CTA owns
+    const int slot_bytes = 128 * cols * 4;     // one source split's slice, FP32
+    const int row_bytes = cols * 4;
+    const uint32_t base = smem_addr(ring);
+    cluster_sync();  // every main loop is done: all rings are free to receive
+    if (warp >= 2 && split_ready) {
+      // ---- push: TMEM -> owner CTA's shared memory, slot = this CTA's split ----
+      tc_fence_after_sync();
+      const int quarter = warp & 3;
+      const uint32_t row = static_cast<uint32_t>(quarter * 32) + lane;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + c, v);
+        tmem_ld_wait();
+        const int owner = c / cols;            // 32-column chunks never straddle two owners
+        const int local = c - owner * cols;    // first column inside the owner's slice
+        const uint32_t dst = map_to_rank(
+            base + split * slot_bytes + row * row_bytes, rank + 2u * static_cast<uint32_t>(owner));
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t chunk = static_cast<uint32_t>(local / 4 + j);
+          st_dsmem_v4(dst + ((chunk ^ (row & 7u)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                      v[4 * j + 3]);
+        }
+      }
+    }
+    cluster_sync();  // every slice has arrived
+    // ---- reduce locally in split order and store FP16 C ----
+    const int chunks = cols / 4;
     int pm, pn;
     grouped_tile(pair, args.tiles_m, args.tiles_n, args.group_m, pm, pn);
     const int row_base = pm * 256 + static_cast<int>(rank) * 128;
     const int col_base = pn * BN + split * cols;
-    const uint32_t base = smem_addr(ring);
     const bool vec = (split_args.ldc % 4 == 0) &&
                      ((reinterpret_cast<uintptr_t>(split_args.c) & 7) == 0);
     for (int i = threadIdx.x; i < 128 * chunks; i += blockDim.x) {
       const uint32_t row = static_cast<uint32_t>(i / chunks);
-      const uint32_t chunk = static_cast<uint32_t>(split * chunks + i % chunks);
-      const uint32_t offset = row * (BN * 4) + ((chunk ^ (row & 7u)) << 4);
-      float4 acc = ld_dsmem_f32x4(map_to_rank(base + offset, rank));
+      const uint32_t chunk = static_cast<uint32_t>(i % chunks);
+      const uint32_t offset = row * row_bytes + ((chunk ^ (row & 7u)) << 4);
+      float4 acc = ld_shared_f32x4(base + offset);
       for (int s2 = 1; s2 < splits; ++s2) {
-        const float4 v = ld_dsmem_f32x4(map_to_rank(base + offset, rank + 2u * s2));
+        const float4 v = ld_shared_f32x4(base + s2 * slot_bytes + offset);
         acc.x += v.x;
         acc.y += v.y;
         acc.z += v.z;
         acc.w += v.w;
       }
       const int m = row_base + static_cast<int>(row);
-      const int n = col_base + (i % chunks) * 4;
+      const int n = col_base + static_cast<int>(chunk) * 4;
       if (m < args.m) {
         __half* dst = split_args.c + static_cast<int64_t>(m) * split_args.ldc + n;
         if (vec && n + 3 < args.n) {

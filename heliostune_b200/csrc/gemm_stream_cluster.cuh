@@ -4,11 +4,13 @@
 // UMMA N = MP rows of A), with two changes for small M:
 //   * a CTA may own NA = 2 column atoms (256 columns of C): both UMMAs share the A^T tile of a
 //     stage, halving the A bytes each CTA pulls per byte of B;
-//   * the S CTAs that split one column tile's K range form a thread-block cluster (1, S, 1).
-//     After the main loop every CTA parks its FP32 accumulator in its own shared memory; after a
-//     cluster barrier CTA r sums columns [r*NT/S, (r+1)*NT/S) of all S partials through
-//     distributed shared memory in split order 0..S-1 and writes FP16 C. No workspace, no second
-//     kernel, no atomics; the result is bitwise reproducible.
+//   * the S CTAs that split one column tile's K range form a thread-block cluster (1, S, 1);
+//     CTA r owns columns [r*NT/S, (r+1)*NT/S) of the tile. Once every CTA's main loop is done
+//     (cluster barrier: all rings drained), each CTA pushes every column slice of its FP32
+//     accumulator from TMEM into the owner's shared memory (remote stores, slot = source split);
+//     after a second barrier each owner sums its S slots in split order 0..S-1 from local shared
+//     memory and writes FP16 C. No workspace, no second kernel, no atomics; the result is
+//     bitwise reproducible.
 // With S = 1 the epilogue writes C straight from TMEM.
 #pragma once
 
@@ -178,77 +180,81 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     umma_commit(mma_done);
     if (!mbar_wait(mma_done, 0, nullptr, 200000000ull)) atomicOr(args.status, kStatusDrainTimeout);
   } else if (warp >= 2) {
-    // ---------------- epilogue: TMEM -> C (one split) or -> own shared memory ----------------
+    // ---------------- epilogue: wait for the accumulator ----------------
+    have_result = __all_sync(0xffffffffu, mbar_wait(tmem_full, 0, abort_flag));
+    if (!have_result && lane == 0) raise_abort(args.status, abort_flag, kStatusEpilogueTimeout);
+  }
+
+  constexpr int kChunk = MP >= 32 ? 32 : 16;
+  const int splits = args.splits;
+  const int cols = S::kNT / splits;           // columns of C each CTA of the cluster owns
+  const int slot_bytes = MP * cols * 4;       // one source split's slice, FP32 [MP][cols]
+  const uint32_t base = smem_addr(partial);
+  if (splits > 1) cluster_sync();  // every main loop is done: all rings can receive
+  if (warp >= 2 && have_result) {
+    // ---- TMEM -> C (one split) or -> the owner's shared memory (remote stores) ----
+    tc_fence_after_sync();
     const int quarter = warp & 3;
-    const bool ready = __all_sync(0xffffffffu, mbar_wait(tmem_full, 0, abort_flag));
-    if (!ready) {
-      if (lane == 0) raise_abort(args.status, abort_flag, kStatusEpilogueTimeout);
-    } else {
-      tc_fence_after_sync();
-      have_result = true;
-      constexpr int kChunk = MP >= 32 ? 32 : 16;
 #pragma unroll 1
-      for (int a = 0; a < NA; ++a) {
-        const int nl = a * 128 + quarter * 32 + static_cast<int>(lane);
-        const int n = n0 + nl;
-        const uint32_t lane_addr =
-            tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * MP;
+    for (int a = 0; a < NA; ++a) {
+      const int nl = a * 128 + quarter * 32 + static_cast<int>(lane);
+      const int n = n0 + nl;
+      const int owner = nl / cols;
+      const uint32_t dst = splits > 1 ? map_to_rank(base + split * slot_bytes + (nl - owner * cols) * 4,
+                                                    static_cast<uint32_t>(owner))
+                                      : 0u;
+      const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * MP;
 #pragma unroll 1
-        for (int c0 = 0; c0 < MP; c0 += kChunk) {
-          if (c0 >= args.m) break;  // warp-uniform
-          float v[kChunk];
-          if constexpr (kChunk == 32) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(lane_addr + c0, r);
-            tmem_ld_wait();
+      for (int c0 = 0; c0 < MP; c0 += kChunk) {
+        if (c0 >= args.m) break;  // warp-uniform
+        uint32_t r[kChunk];
+        if constexpr (kChunk == 32) {
+          tmem_ld_32x32b_x32(lane_addr + c0, r);
+        } else {
+          tmem_ld_32x32b_x16(lane_addr + c0, r);
+        }
+        tmem_ld_wait();
+        if (splits == 1) {
+          if (n < args.n) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          } else {
-            uint32_t r[16];
-            tmem_ld_32x32b_x16(lane_addr + c0, r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-          }
-          if (args.splits == 1) {
-            if (n < args.n) {
-#pragma unroll
-              for (int j = 0; j < kChunk; ++j) {
-                const int m = c0 + j;
-                if (m < args.m) args.c[static_cast<int64_t>(m) * args.ldc + n] = __float2half_rn(v[j]);
-              }
+            for (int j = 0; j < kChunk; ++j) {
+              const int m = c0 + j;
+              if (m < args.m) args.c[static_cast<int64_t>(m) * args.ldc + n] = __float2half_rn(__uint_as_float(r[j]));
             }
-          } else {
+          }
+        } else {
 #pragma unroll
-            for (int j = 0; j < kChunk; ++j) partial[(c0 + j) * S::kNT + nl] = v[j];
+          for (int j = 0; j < kChunk; ++j) {
+            if (c0 + j < args.m) {
+              asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(dst + (c0 + j) * cols * 4), "r"(r[j])
+                           : "memory");
+            }
           }
         }
       }
     }
   }
 
-  if (args.splits > 1) {
-    // ---------------- in-cluster reduction over the S splits ----------------
-    cluster_sync();  // every CTA's partial is in its shared memory
+  if (splits > 1) {
+    cluster_sync();  // every slice has arrived
+    // ---- reduce locally in split order and write FP16 C ----
     const int rank = static_cast<int>(cluster_ctarank());
-    const int cols = S::kNT / args.splits;  // columns this CTA reduces
     const int quads = cols / 4;
     const int items = args.m * quads;
-    const uint32_t base = smem_addr(partial);
     const bool vec_store = (args.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(args.c) & 7) == 0);
     for (int i = threadIdx.x; i < items; i += blockDim.x) {
       const int m = i / quads;
-      const int nl = rank * cols + (i % quads) * 4;
-      const uint32_t offset = static_cast<uint32_t>((m * S::kNT + nl) * 4);
-      float4 acc = ld_dsmem_f32x4(map_to_rank(base + offset, 0));
-      for (int s = 1; s < args.splits; ++s) {
-        const float4 v = ld_dsmem_f32x4(map_to_rank(base + offset, static_cast<uint32_t>(s)));
+      const int q = i % quads;
+      const uint32_t offset = static_cast<uint32_t>((m * cols + q * 4) * 4);
+      float4 acc = ld_shared_f32x4(base + offset);
+      for (int s = 1; s < splits; ++s) {
+        const float4 v = ld_shared_f32x4(base + s * slot_bytes + offset);
         acc.x += v.x;
         acc.y += v.y;
         acc.z += v.z;
         acc.w += v.w;
       }
-      const int n = n0 + nl;
+      const int n = n0 + rank * cols + q * 4;
       __half* dst = args.c + static_cast<int64_t>(m) * args.ldc + n;
       if (vec_store && n + 3 < args.n) {
         __half2 lo = __floats2half2_rn(acc.x, acc.y);
@@ -262,7 +268,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         for (int j = 0; j < 4 && n + j < args.n; ++j) dst[j] = __float2half_rn(vals[j]);
       }
     }
-    cluster_sync();  // peers finished reading this CTA's shared memory
   }
   (void)have_result;
 

@@ -277,6 +277,23 @@ __device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t cluster_addr) {
   return v;
 }
 
+// Stores four 32-bit values to (possibly another CTA's) shared memory at a shared::cluster address.
+__device__ __forceinline__ void st_dsmem_v4(uint32_t cluster_addr, uint32_t a, uint32_t b,
+                                            uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(a),
+               "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ float4 ld_shared_f32x4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 // Whole-cluster execution barrier (all threads of all CTAs of the cluster). The warp is
 // reconverged first: the .aligned barrier needs every lane at the same instruction, and callers
 // reach it from role branches that only lane 0 of a warp entered.
