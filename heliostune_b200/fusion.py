@@ -15,6 +15,7 @@ from collections.abc import Callable
 import torch
 
 from heliostune_b200 import _native
+from heliostune_b200.action_configs import ActionCandidate
 from heliostune_b200.kernel import _stream
 
 DEFAULT_EPS = 1e-6
@@ -47,6 +48,30 @@ def rmsnorm(x: torch.Tensor, gamma: torch.Tensor, eps: float = DEFAULT_EPS) -> t
             )
         )
     return y
+
+
+def rmsnorm_matmul(
+    x: torch.Tensor,
+    gamma: torch.Tensor,
+    w: torch.Tensor,
+    candidate: ActionCandidate,
+    eps: float = DEFAULT_EPS,
+) -> torch.Tensor:
+    """``RMSNorm(x; gamma, eps) @ W`` -- the RMSNorm feeding the QKV projection.
+
+    The normalised rows are produced exactly as the reference's formula rounds them,
+    ``fp16((x * rsqrt(mean(x^2) + eps)) * gamma)``, into a per-call workspace by the RMSNorm
+    kernel, and the GEMM candidate consumes that workspace on the same stream. Materialising the
+    ``[M, K]`` FP16 rows costs ``4MK`` bytes of HBM traffic (write + read) next to the GEMM's
+    ``2(MK + KN + MN)``; rescaling the A tiles inside the GEMM instead would put the same work
+    on the shared-memory path the tensor-core main loop is limited by.
+    """
+    from heliostune_b200.action_expansion import launch
+
+    if w.ndim != 2 or w.shape[0] != x.shape[1]:
+        raise ValueError(f"incompatible shapes: x {tuple(x.shape)} and W {tuple(w.shape)}")
+    normalised = rmsnorm(x, gamma, eps)
+    return launch(normalised, w, candidate)
 
 
 RMSNORM_ENTRYPOINTS: tuple[str, ...] = ("heliostune_b200::rmsnorm",)

@@ -51,6 +51,28 @@ def test_full_size_against_the_fp32_formula(rows: int, hidden: int) -> None:
     assert torch.equal(x.view(torch.int16), x0.view(torch.int16))
 
 
+@pytest.mark.parametrize("rows", (1, 128, 4096))
+def test_rmsnorm_feeding_the_qkv_gemm(rows: int) -> None:
+    from heliostune_b200.action_configs import b200_candidates_for
+    from heliostune_b200.action_expansion import fp32_reference
+    from heliostune_b200.configs import Workload
+    from heliostune_b200.fusion import rmsnorm_matmul
+    from tests.gpu_helpers import assert_gemm_parity
+
+    x, gamma = _inputs(rows, 4096, seed=rows)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    w = (torch.randn((4096, 6144), generator=g, device="cuda") / 64).to(torch.float16)
+    xf = x.float()
+    normalised = (xf * torch.rsqrt((xf * xf).mean(dim=-1, keepdim=True) + 1e-6) * gamma.float()).to(torch.float16)
+    workload = Workload(m=rows, n=6144, k=4096, model="llama-3-8b", projection="attention-qkv", regime="m")
+    for candidate in b200_candidates_for(workload)[:4]:
+        out = rmsnorm_matmul(x, gamma, w, candidate)
+        assert_gemm_parity(out, normalised, w)
+        # and against the FP32 product of the unrounded normalised rows
+        exact = fp32_reference((xf * torch.rsqrt((xf * xf).mean(dim=-1, keepdim=True) + 1e-6) * gamma.float()), w.float())
+        assert (out.float() - exact).abs().max().item() <= 1e-2 * exact.abs().max().item()
+
+
 def test_registry_is_closed() -> None:
     assert load_rmsnorm("heliostune_b200::rmsnorm") is rmsnorm
     with pytest.raises(KeyError):
