@@ -464,8 +464,18 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
     g = torch.Generator(device=device).manual_seed(1000 + rank)
     b_shard = (torch.randn((w.k, shard.cols), generator=g, device=device) / math.sqrt(w.k)).to(torch.float16)
 
-    def step(events):
-        return column_parallel_matmul(a, b_shard, phase_events=events)
+    if args.fused:
+        from heliostune_b200.column_parallel import FusedColumnParallel
+
+        fused = FusedColumnParallel(w.m, w.n, device=device)
+
+        def step(events):
+            return fused(a, b_shard, phase_events=events)
+    else:
+        fused = None
+
+        def step(events):
+            return column_parallel_matmul(a, b_shard, phase_events=events)
 
     for _ in range(args.warmup):
         step(None)
@@ -533,10 +543,16 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
         },
         "step_roofline_frac": round(t_roof / (step_ms / 1e3), 4),
         "gather_gbs": round(gather_bytes / (gather_ms / 1e3) / 1e9, 1) if world > 1 else None,
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": (1 if args.fused else 2) * args.steps,
         "clocks": sampler.summary(epoch0, epoch1),
         "status_bits": _native.status(local_rank),
     }
+    if args.fused:
+        result["config"]["exchange"] = "fused: GEMM epilogue stores every tile to all ranks over NVLink"
+        result["gemm_ms_note"] = "fused mode: gemm_ms = barrier + GEMM with overlapped peer stores"
+        fused.close()
+    else:
+        result["config"]["exchange"] = "NCCL all-gather + column assembly"
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -776,6 +792,7 @@ def main() -> None:
     parser.add_argument("--skip-cublas", action="store_true", help="profiling runs: no cuBLAS passes")
     parser.add_argument("--force", default=None, help="profiling runs: one candidate key for every shape")
     parser.add_argument("--tag", default=None, help="name of the --detail file")
+    parser.add_argument("--fused", action="store_true", help="colpar: all-gather fused into the GEMM")
     args = parser.parse_args()
     if args.warmup < 3 and args.impl == "ours" and not args.shapes:
         print("note: fewer than 3 warm-up passes", file=sys.stderr)

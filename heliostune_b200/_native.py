@@ -59,6 +59,10 @@ EXPORTED_SYMBOLS = (
     "hst_probe_wait_timeout",
     "hst_matmul_split_k_noalloc",
     "hst_column_assemble",
+    "hst_matmul_pair_fanout",
+    "hst_ipc_export",
+    "hst_ipc_import",
+    "hst_ipc_close",
 )
 
 
@@ -145,6 +149,13 @@ def _declare(lib: ctypes.CDLL) -> None:
         "hst_status": ([ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int], ctypes.c_int),
         "hst_probe_wait_timeout": ([_u64, _ptr], ctypes.c_int),
         "hst_column_assemble": ([_ptr, _ptr, _i64, _i64, _i64, _i64, _ptr], ctypes.c_int),
+        "hst_ipc_export": ([_ptr, _ptr, ctypes.POINTER(_u64)], ctypes.c_int),
+        "hst_ipc_import": ([_ptr, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+        "hst_ipc_close": ([_ptr], ctypes.c_int),
+        "hst_matmul_pair_fanout": (
+            [_i32] * 4 + [_ptr, _ptr, ctypes.POINTER(ctypes.c_void_p), _i32, _i32, _i64, _i64, _i64, _ptr],
+            ctypes.c_int,
+        ),
         "hst_matmul_split_k_noalloc": (
             [_i32] * 6 + [_ptr, _i64, _i64, _ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i64, _ptr],
             ctypes.c_int,

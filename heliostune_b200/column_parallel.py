@@ -78,6 +78,112 @@ def assemble_columns(gathered: torch.Tensor, out: torch.Tensor | None = None) ->
     return out
 
 
+class FusedColumnParallel:
+    """Column-parallel GEMM whose all-gather is fused into the GEMM epilogue.
+
+    Every rank allocates its full output ``C [M, N]`` once (``torch.empty``), exports its CUDA
+    IPC handle, and maps every peer's output (``hst_ipc_*``). A call runs the persistent CTA-pair
+    GEMM on this rank's column slice; each finished sub-tile goes to the local C by TMA and to
+    every peer's C by coalesced NVLink stores while the next tiles compute
+    (``hst_matmul_pair_fanout``). NCCL barriers before and after the launch order the ranks: no
+    peer writes into a C that is still being read, and C is complete when the call returns.
+    The returned tensor is this object's buffer and is overwritten by the next call.
+    """
+
+    def __init__(
+        self,
+        m: int,
+        n_total: int,
+        *,
+        group: dist.ProcessGroup | None = None,
+        candidate: ActionCandidate = COLUMN_PARALLEL_CANDIDATE,
+        device: torch.device | None = None,
+    ) -> None:
+        import ctypes
+
+        if not isinstance(candidate.config, PairConfig):
+            raise ValueError("the fused column-parallel GEMM runs the CTA-pair kernel")
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.shard = ColumnShard(n_total, self.world, self.rank)
+        self.candidate = candidate
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.out = torch.empty((m, n_total), dtype=torch.float16, device=self.device)
+        self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+        lib = _native.library()
+        handle = (ctypes.c_char * 64)()
+        offset = ctypes.c_uint64(0)
+        _native.check(lib.hst_ipc_export(self.out.data_ptr(), handle, ctypes.byref(offset)))
+        mine = (bytes(handle), offset.value)
+        gathered: list[object] = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(gathered, mine, group=group)
+        else:
+            gathered = [mine]
+        self._bases: list[int] = []
+        pointers = []
+        for q, (raw, off) in enumerate(gathered):  # type: ignore[misc]
+            if q == self.rank:
+                pointers.append(self.out.data_ptr())
+                continue
+            base = ctypes.c_void_p()
+            _native.check(lib.hst_ipc_import(raw, ctypes.byref(base)))
+            self._bases.append(base.value)
+            pointers.append(base.value + off)
+        self._pointers = (ctypes.c_void_p * self.world)(*pointers)
+
+    def _barrier(self) -> None:
+        if self.world > 1:
+            dist.all_reduce(self._flag, group=self.group)
+
+    def __call__(
+        self,
+        a: torch.Tensor,
+        b_shard: torch.Tensor,
+        phase_events: list[torch.cuda.Event] | None = None,
+    ) -> torch.Tensor:
+        config = self.candidate.config
+        m, k = a.shape
+        if b_shard.shape != (k, self.shard.cols) or m != self.out.shape[0]:
+            raise ValueError("operand shapes do not match this column-parallel plan")
+        if not (a.is_contiguous() and b_shard.is_contiguous()):
+            raise ValueError("operands must be row-major contiguous")
+        if phase_events:
+            phase_events[0].record()
+        self._barrier()  # every rank is done reading the previous result
+        _native.check(
+            _native.library().hst_matmul_pair_fanout(
+                config.block_n,
+                config.block_k,
+                config.num_stages,
+                config.group_m,
+                a.data_ptr(),
+                b_shard.data_ptr(),
+                self._pointers,
+                self.world,
+                self.rank,
+                m,
+                self.shard.n_total,
+                k,
+                torch.cuda.current_stream(self.device).cuda_stream,
+            )
+        )
+        if phase_events:
+            phase_events[1].record()
+        self._barrier()  # every rank's slices have landed everywhere
+        if phase_events:
+            phase_events[2].record()
+        return self.out
+
+    def close(self) -> None:
+        lib = _native.library()
+        torch.cuda.synchronize(self.device)
+        for base in self._bases:
+            _native.check(lib.hst_ipc_close(base))
+        self._bases = []
+
+
 def _default_gemm(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     from heliostune_b200.action_expansion import launch
 

@@ -8,6 +8,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
+#include <cstring>
 #include <string>
 
 #include "../../include/heliostune_b200.h"
@@ -507,7 +508,7 @@ int dispatch_tile(const DeviceState& dev, const Plan& p, const Operands& o, bool
 
 template <int BN, int BK, bool SPLIT>
 int launch_pair(const DeviceState& dev, const Operands& o, int stages, int group_m, int splits,
-                int kb_per_split, cudaStream_t stream) {
+                int kb_per_split, cudaStream_t stream, const PairFanoutArgs* fanout_in = nullptr) {
   using S = PairShape<BN, BK>;
   static std::atomic<uint64_t> smem_done{0};
   HST_TRY(allow_smem(pair_gemm_kernel<BN, BK, SPLIT>, smem_done));
@@ -533,6 +534,8 @@ int launch_pair(const DeviceState& dev, const Operands& o, int stages, int group
   args.group_m = group_m;
   args.stages = stages;
   args.status = dev.status;
+  PairFanoutArgs fanout = {};
+  if (fanout_in != nullptr) fanout = *fanout_in;
   PairSplitArgs split_args;
   split_args.splits = splits;
   split_args.kb_per_split = kb_per_split;
@@ -553,7 +556,8 @@ int launch_pair(const DeviceState& dev, const Operands& o, int stages, int group
   attr[0].val.clusterDim.z = 1;
   lc.attrs = attr;
   lc.numAttrs = 1;
-  HST_CUDA(cudaLaunchKernelEx(&lc, pair_gemm_kernel<BN, BK, SPLIT>, ma_, mb_, mc_, args, split_args));
+  HST_CUDA(cudaLaunchKernelEx(&lc, pair_gemm_kernel<BN, BK, SPLIT>, ma_, mb_, mc_, args, split_args,
+                              fanout));
   return HST_OK;
 }
 
@@ -918,6 +922,56 @@ int hst_matmul_pair(int32_t block_n, int32_t block_k, int32_t num_stages, int32_
                    workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
+int hst_matmul_pair_fanout(int32_t block_n, int32_t block_k, int32_t num_stages, int32_t group_m,
+                           const void* a, const void* b_slice, void* const* c_ranks, int32_t world,
+                           int32_t rank, int64_t m, int64_t n_total, int64_t k, void* stream) {
+  if (world < 1 || world > kMaxPeers + 1 || rank < 0 || rank >= world)
+    return fail(HST_ERR_INVALID, "world %d / rank %d out of range (at most %d ranks)", world, rank,
+                kMaxPeers + 1);
+  if (n_total % world != 0) return fail(HST_ERR_INVALID, "N must split evenly over the ranks");
+  const int64_t cols = n_total / world;
+  if (cols % 8 != 0 || k % 8 != 0)
+    return fail(HST_ERR_INVALID, "the column slice and K must be multiples of 8");
+  if (c_ranks == nullptr || a == nullptr || b_slice == nullptr)
+    return fail(HST_ERR_INVALID, "null pointer");
+  HST_TRY(check_problem(a, b_slice, c_ranks[rank], m, cols, k, n_total));
+  DeviceState* dev = nullptr;
+  HST_TRY(device_state(&dev));
+  const hst_gemm_config cfg{HST_FAMILY_PAIR, 256, block_n, block_k, 4, num_stages, group_m, 1};
+  const View va{static_cast<const __half*>(a), m, k, k, 1};
+  const View vb{static_cast<const __half*>(b_slice), k, cols, cols, 1};
+  Plan p;
+  HST_TRY(make_plan(&cfg, va, vb, m, cols, k, dev->sm_count, &p));
+  if (p.pack_a || p.pack_b) return fail(HST_ERR_INVALID, "operands must be 16-byte aligned row-major");
+  if (m == 0) return HST_OK;
+  PairFanoutArgs fanout = {};
+  fanout.ldc = n_total;
+  for (int q = 0; q < world; ++q) {
+    if (q == rank) continue;
+    if (c_ranks[q] == nullptr) return fail(HST_ERR_INVALID, "null peer output");
+    fanout.peers[fanout.count++] =
+        reinterpret_cast<uint64_t>(static_cast<__half*>(c_ranks[q]) + rank * cols);
+  }
+  Operands o;
+  o.m = static_cast<int>(m);
+  o.n = static_cast<int>(cols);
+  o.k = static_cast<int>(k);
+  o.a = va.ptr;
+  o.lda = k;
+  o.b = vb.ptr;
+  o.ldb = cols;
+  o.c = static_cast<__half*>(c_ranks[rank]) + rank * cols;
+  o.ldc = n_total;
+  if ((reinterpret_cast<uintptr_t>(o.c) & 15) != 0 || n_total % 8 != 0)
+    return fail(HST_ERR_INVALID, "output rows must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p.bn == 256 && p.bk == 64) return launch_pair<256, 64, false>(*dev, o, p.stages, p.group_m, 1, 0, s, &fanout);
+  if (p.bn == 128 && p.bk == 64) return launch_pair<128, 64, false>(*dev, o, p.stages, p.group_m, 1, 0, s, &fanout);
+  if (p.bn == 256 && p.bk == 128) return launch_pair<256, 128, false>(*dev, o, p.stages, p.group_m, 1, 0, s, &fanout);
+  if (p.bn == 128 && p.bk == 128) return launch_pair<128, 128, false>(*dev, o, p.stages, p.group_m, 1, 0, s, &fanout);
+  return fail(HST_ERR_UNSUPPORTED, "no pair kernel for N %d, K %d", p.bn, p.bk);
+}
+
 int hst_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* y, int64_t ldy,
                 int64_t rows, int64_t hidden, float eps, void* stream) {
   if (rows < 0 || hidden < 1) return fail(HST_ERR_INVALID, "rows must be >= 0 and hidden >= 1");
@@ -972,6 +1026,47 @@ int hst_column_assemble(const void* src, void* dst, int64_t parts, int64_t rows,
       static_cast<const __half*>(src), static_cast<__half*>(dst), parts, rows, cols_per_part, ldd,
       vec8 ? 1 : 0);
   HST_CUDA(cudaGetLastError());
+  return HST_OK;
+}
+
+// ---- peer mappings for the fused column-parallel GEMM (CUDA IPC, no multicast objects) ----
+
+typedef CUresult (*PfnMemGetAddressRange)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+int hst_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out) {
+  if (ptr == nullptr || handle_out == nullptr || offset_out == nullptr)
+    return fail(HST_ERR_INVALID, "null pointer");
+  static PfnMemGetAddressRange get_range = nullptr;
+  if (get_range == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    HST_CUDA(cudaGetDriverEntryPointByVersion("cuMemGetAddressRange",
+                                              reinterpret_cast<void**>(&get_range), 12000,
+                                              cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || get_range == nullptr)
+      return fail(HST_ERR_CUDA, "cuMemGetAddressRange unavailable");
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (get_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(HST_ERR_CUDA, "cuMemGetAddressRange failed");
+  cudaIpcMemHandle_t handle;
+  HST_CUDA(cudaIpcGetMemHandle(&handle, reinterpret_cast<void*>(base)));
+  memcpy(handle_out, &handle, sizeof(handle));
+  *offset_out = reinterpret_cast<uint64_t>(ptr) - static_cast<uint64_t>(base);
+  return HST_OK;
+}
+
+int hst_ipc_import(const void* handle, void** base_out) {
+  if (handle == nullptr || base_out == nullptr) return fail(HST_ERR_INVALID, "null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  HST_CUDA(cudaIpcOpenMemHandle(base_out, h, cudaIpcMemLazyEnablePeerAccess));
+  return HST_OK;
+}
+
+int hst_ipc_close(void* base) {
+  if (base == nullptr) return fail(HST_ERR_INVALID, "null pointer");
+  HST_CUDA(cudaIpcCloseMemHandle(base));
   return HST_OK;
 }
 

@@ -53,6 +53,16 @@ struct PairShape {
   }
 };
 
+// Column-parallel fan-out of the persistent pair kernel: every finished 64-column sub-tile of
+// this rank's C slice is also written, with coalesced 16-byte stores, into the same columns of
+// the other ranks' C (peer pointers over NVLink). The local copy goes through the TMA store.
+constexpr int kMaxPeers = 8;
+struct PairFanoutArgs {
+  uint64_t peers[kMaxPeers];  // other ranks' C base + this rank's column offset (elements)
+  int count;                  // number of peers (0 = no fan-out)
+  int64_t ldc;                // row stride of every rank's full C, elements
+};
+
 struct PairSplitArgs {
   int splits;        // cluster extent along y (1 = persistent mode)
   int kb_per_split;  // K blocks of one split
@@ -65,7 +75,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     pair_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                      const __grid_constant__ CUtensorMap map_b,
                      const __grid_constant__ CUtensorMap map_c, const TileArgs args,
-                     const PairSplitArgs split_args) {
+                     const PairSplitArgs split_args, const __grid_constant__ PairFanoutArgs fanout) {
   using S = PairShape<BN, BK>;
   static_assert(!SPLIT || BN * 128 * 4 <= 6 * 32768, "the FP32 partial reuses the ring");
   extern __shared__ uint8_t smem_raw[];
@@ -268,6 +278,28 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           tma_store_2d(&map_c, dst, n0 + c * 64, row0);
           bulk_commit_group();
         }
+        if (fanout.count > 0) {
+          // Each lane moves 8 of the sub-tile's 256 16-byte chunks; one shared-memory read per
+          // chunk feeds every peer. Rows and columns past the slice are skipped.
+          const uint32_t src = smem_addr(dst);
+#pragma unroll 1
+          for (int i = static_cast<int>(lane); i < 256; i += 32) {
+            const int r = i >> 3, ch = i & 7;
+            const int m = row0 + r, n = n0 + c * 64 + ch * 8;
+            if (m >= args.m || n >= args.n) continue;
+            const float4 v = ld_shared_f32x4(src + r * 128 + ((ch ^ (r & 7)) << 4));
+            const bool full8 = n + 8 <= args.n;
+            for (int q = 0; q < fanout.count; ++q) {
+              __half* out = reinterpret_cast<__half*>(fanout.peers[q]) + static_cast<int64_t>(m) * fanout.ldc + n;
+              if (full8) {
+                *reinterpret_cast<float4*>(out) = v;
+              } else {
+                const __half* h = reinterpret_cast<const __half*>(&v);
+                for (int j = 0; j < 8 && n + j < args.n; ++j) out[j] = h[j];
+              }
+            }
+          }
+        }
         buf ^= 1;
       }
       tc_fence_before_sync();
@@ -285,6 +317,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       }
     }
     if (lane == 0) bulk_wait_group<0>();
+    if (fanout.count > 0) __threadfence_system();  // peer stores are visible before exit
     __syncwarp();
   }
 

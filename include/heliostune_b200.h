@@ -128,6 +128,25 @@ int hst_matmul_pair(int32_t block_n, int32_t block_k, int32_t num_stages, int32_
 int hst_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* y, int64_t ldy,
                 int64_t rows, int64_t hidden, float eps, void* stream);
 
+/* Fused column-parallel GEMM (no reference counterpart). Rank `rank` of `world` (<= 9) holds
+ * A [m, k] and its column slice B_r [k, n_total / world], both row-major contiguous. c_ranks[q]
+ * is rank q's full output C [m, n_total] (row-major, ldc = n_total) as mapped into this process
+ * (e.g. symmetric memory); the CTA-pair GEMM writes C_r = A B_r into columns
+ * [rank * n_total / world, (rank + 1) * n_total / world) of its own C by TMA and of every peer's
+ * C by coalesced peer stores as each tile finishes, so the exchange overlaps the GEMM. The
+ * caller orders the ranks afterwards (a cross-rank barrier on the stream) before reading C. */
+int hst_matmul_pair_fanout(int32_t block_n, int32_t block_k, int32_t num_stages, int32_t group_m,
+                           const void* a, const void* b_slice, void* const* c_ranks, int32_t world,
+                           int32_t rank, int64_t m, int64_t n_total, int64_t k, void* stream);
+
+/* Peer mappings for hst_matmul_pair_fanout (CUDA IPC; no multicast objects). hst_ipc_export
+ * writes the 64-byte IPC handle of the allocation containing `ptr` and ptr's offset in it;
+ * another process opens it with hst_ipc_import (the mapped base) and releases it with
+ * hst_ipc_close. */
+int hst_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out);
+int hst_ipc_import(const void* handle, void** base_out);
+int hst_ipc_close(void* base);
+
 /* Column-parallel assembly (no reference counterpart: the reference has no multi-GPU path).
  * dst[r, p * cols_per_part + c] = src[p][r][c] for the rank-ordered [parts][rows][cols_per_part]
  * chunks an all-gather of per-rank C slices returns; dst has row stride ldd. */

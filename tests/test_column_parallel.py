@@ -93,3 +93,52 @@ def test_assembly_kernel_and_single_rank_path() -> None:
     c = column_parallel_matmul(a, b)
     assert_gemm_parity(c, a, b)
     assert np.isfinite(c.float().cpu().numpy()).all()
+
+
+def _fused_rank(rank: int, world: int, port: int, queue) -> None:  # type: ignore[no-untyped-def]
+    from datetime import timedelta
+
+    from heliostune_b200.action_expansion import fp32_reference
+    from heliostune_b200.column_parallel import FusedColumnParallel
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    device = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=device)
+    try:
+        results = []
+        for m, k, n in ((1000, 1032, 2 * 1024), (512, 4096, 2 * 1536)):
+            g = torch.Generator(device=device).manual_seed(m + k)
+            a = (torch.randn((m, k), generator=g, device=device) / k**0.5).to(torch.float16)
+            b = (torch.randn((k, n), generator=g, device=device) / k**0.5).to(torch.float16)
+            shard = ColumnShard(n, world, rank)
+            fused = FusedColumnParallel(m, n, device=device)
+            expected = fp32_reference(a, b)
+            plain = column_parallel_matmul(a, shard.take(b))
+            for _ in range(2):  # the second call reuses the mapped outputs
+                c = fused(a, shard.take(b)).clone()
+                close = bool(torch.allclose(c.float(), expected, atol=1e-2, rtol=1e-2))
+                results.append(close and bool(torch.equal(c, plain)))
+            fused.close()
+        queue.put((rank, all(results)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_fused_column_parallel_on_two_gpus() -> None:
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_rank, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    results = [queue.get(timeout=10) for _ in range(world)]
+    assert sorted(r for r, _ in results) == [0, 1]
+    assert all(ok for _, ok in results)
