@@ -464,7 +464,7 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
     g = torch.Generator(device=device).manual_seed(1000 + rank)
     b_shard = (torch.randn((w.k, shard.cols), generator=g, device=device) / math.sqrt(w.k)).to(torch.float16)
 
-    if args.fused:
+    if args.exchange == "fused" and world > 1:
         from heliostune_b200.column_parallel import FusedColumnParallel
 
         fused = FusedColumnParallel(w.m, w.n, device=device)
@@ -543,11 +543,11 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
         },
         "step_roofline_frac": round(t_roof / (step_ms / 1e3), 4),
         "gather_gbs": round(gather_bytes / (gather_ms / 1e3) / 1e9, 1) if world > 1 else None,
-        "gpu_launches": (1 if args.fused else 2) * args.steps,
+        "gpu_launches": (1 if fused is not None or world == 1 else 2) * args.steps,
         "clocks": sampler.summary(epoch0, epoch1),
         "status_bits": _native.status(local_rank),
     }
-    if args.fused:
+    if fused is not None:
         result["config"]["exchange"] = "fused: GEMM epilogue stores every tile to all ranks over NVLink"
         result["gemm_ms_note"] = "fused mode: gemm_ms = barrier + GEMM with overlapped peer stores"
         fused.close()
@@ -792,7 +792,12 @@ def main() -> None:
     parser.add_argument("--skip-cublas", action="store_true", help="profiling runs: no cuBLAS passes")
     parser.add_argument("--force", default=None, help="profiling runs: one candidate key for every shape")
     parser.add_argument("--tag", default=None, help="name of the --detail file")
-    parser.add_argument("--fused", action="store_true", help="colpar: all-gather fused into the GEMM")
+    parser.add_argument(
+        "--exchange",
+        choices=("fused", "nccl"),
+        default="fused",
+        help="colpar: all-gather fused into the GEMM epilogue, or NCCL all-gather + assembly",
+    )
     args = parser.parse_args()
     if args.warmup < 3 and args.impl == "ours" and not args.shapes:
         print("note: fewer than 3 warm-up passes", file=sys.stderr)

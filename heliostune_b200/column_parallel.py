@@ -215,7 +215,9 @@ def column_parallel_matmul(
     if phase_events:
         phase_events[1].record()
     if world == 1:
-        gathered = local.unsqueeze(0)
+        if phase_events:
+            phase_events[2].record()
+        return local  # one rank: the slice is the whole product
     else:
         rows, cols = local.shape
         flat = torch.empty((world * rows, cols), dtype=local.dtype, device=local.device)
