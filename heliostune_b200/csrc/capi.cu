@@ -350,7 +350,9 @@ int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t 
         splits = 1;
         while (splits < 4 && tiles * splits * 2 <= sms / 2) splits *= 2;
       }
-      while (splits > 1 && (splits > k_blocks || cdiv(k_blocks, cdiv(k_blocks, splits)) != splits))
+      // Each CTA owns at least 64 columns (one TMA-store sub-tile) of the tile.
+      while (splits > 1 && (bn / splits < 64 || splits > k_blocks ||
+                            cdiv(k_blocks, cdiv(k_blocks, splits)) != splits))
         splits /= 2;
       p->splits = splits;
       p->kb_per_split = static_cast<int>(cdiv(k_blocks, splits));
@@ -514,8 +516,9 @@ int launch_pair(const DeviceState& dev, const Operands& o, int stages, int group
   HST_TRY(allow_smem(pair_gemm_kernel<BN, BK, SPLIT>, smem_done));
   while (stages > 2 && S::smem_bytes(stages) > kMaxDynamicSmem) --stages;
   if (SPLIT) {
-    // The parked FP32 partial (128 x BN) reuses the drained ring.
-    while (stages * S::kStageBytes < 128 * BN * 4) ++stages;
+    // The staged outgoing and the incoming FP32 slices reuse the drained ring.
+    const int exchange = 2 * (splits - 1) * 128 * (BN / splits) * 4;
+    while (stages * S::kStageBytes < exchange) ++stages;
   }
   if (S::smem_bytes(stages) > kMaxDynamicSmem)
     return fail(HST_ERR_UNSUPPORTED, "pair tile 256x%dx%d does not fit shared memory", BN, BK);

@@ -18,11 +18,12 @@
 // SPLIT = true (split-K for tile counts far below the SM count): the cluster grows to (2, S):
 // S pairs compute the same 256 x BN tile over S contiguous K ranges. CTA (r, s) owns columns
 // [s*BN/S, (s+1)*BN/S) of its 128 rows. Once every CTA's main loop is done (cluster barrier, so
-// all rings are drained), each CTA pushes every column slice of its FP32 partial from TMEM
-// straight into the owning CTA's shared memory (remote stores, slot = source split, 16-byte
-// chunks swizzled by row); after a second barrier each owner sums its S slots in split order
-// from local shared memory and stores FP16 C. One tile per cluster; no workspace, no atomics,
-// bitwise reproducible.
+// all rings are drained), each CTA stages the column slices it does not own from TMEM into its
+// own shared memory and sends each with one asynchronous bulk copy into the owner's receive
+// slot (completed in bytes on the owner's mbarrier). The owner then adds, in split order, its
+// own slice read straight from TMEM and the S - 1 received slices, and stores FP16 C through
+// the usual staged TMA-store epilogue. One tile per cluster; no workspace, no atomics, bitwise
+// reproducible.
 // No TMA load here feeds more than one CTA's shared memory.
 #pragma once
 
@@ -77,7 +78,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
                      const __grid_constant__ CUtensorMap map_c, const TileArgs args,
                      const PairSplitArgs split_args, const __grid_constant__ PairFanoutArgs fanout) {
   using S = PairShape<BN, BK>;
-  static_assert(!SPLIT || BN * 128 * 4 <= 6 * 32768, "the FP32 partial reuses the ring");
+
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -90,7 +91,8 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   uint64_t* tmem_full = bars + 2 * kMaxStages;
   uint64_t* tmem_empty = tmem_full + 2;
   uint64_t* mma_done = tmem_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* recv_bar = mma_done + 1;  // split mode: the S - 1 incoming slices
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -114,6 +116,12 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       mbar_init(&tmem_empty[b], 8);  // four epilogue warps in each CTA (leader's copy is used)
     }
     mbar_init(mma_done, 1);
+    mbar_init(recv_bar, 1);
+    if (SPLIT) {
+      // Armed before anyone can send: the phase completes once every incoming byte is here.
+      const int slice_bytes = 128 * (BN / split_args.splits) * 4;
+      mbar_arrive_expect_tx(recv_bar, (split_args.splits - 1) * slice_bytes);
+    }
     *abort_flag = 0;
     fence_mbarrier_init();
     tma_prefetch_map(&map_a);
@@ -323,69 +331,106 @@ __global__ void __launch_bounds__(kTileThreads, 1)
 
   if constexpr (SPLIT) {
     const int splits = split_args.splits;
-    const int cols = BN / splits;              // columns each CTA owns
-    const int slot_bytes = 128 * cols * 4;     // one source split's slice, FP32
+    const int cols = BN / splits;                 // columns each CTA owns (>= 64)
+    const int slice_bytes = 128 * cols * 4;       // one 128-row FP32 column slice
     const int row_bytes = cols * 4;
-    const uint32_t base = smem_addr(ring);
-    cluster_sync();  // every main loop is done: all rings are free to receive
-    if (warp >= 2 && split_ready) {
-      // ---- push: TMEM -> owner CTA's shared memory, slot = this CTA's split ----
-      tc_fence_after_sync();
+    uint8_t* outgoing = ring;                     // S - 1 slices this CTA sends
+    uint8_t* incoming = ring + (splits - 1) * slice_bytes;  // S - 1 slices it receives
+    // Slot of split `src` among the S - 1 slices CTA `dst` exchanges (its own is never sent).
+    auto slot_of = [](int src, int dst) { return src < dst ? src : src - 1; };
+    auto slot = [&](int other) { return slot_of(other, split); };
+    cluster_sync();  // every main loop is done: all rings are free
+    if (warp >= 2) {
       const int quarter = warp & 3;
       const uint32_t row = static_cast<uint32_t>(quarter * 32) + lane;
+      const uint32_t lane_tmem = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+      if (split_ready) {
+        tc_fence_after_sync();
+        // ---- stage the slices other CTAs own ----
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + c, v);
-        tmem_ld_wait();
-        const int owner = c / cols;            // 32-column chunks never straddle two owners
-        const int local = c - owner * cols;    // first column inside the owner's slice
-        const uint32_t dst = map_to_rank(
-            base + split * slot_bytes + row * row_bytes, rank + 2u * static_cast<uint32_t>(owner));
+        for (int c = 0; c < BN; c += 32) {
+          const int owner = c / cols;
+          if (owner == split) continue;
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(lane_tmem + c, v);
+          tmem_ld_wait();
+          const uint32_t dst = smem_addr(outgoing + slot(owner) * slice_bytes) + row * row_bytes;
+          const int local = c - owner * cols;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t chunk = static_cast<uint32_t>(local / 4 + j);
-          st_dsmem_v4(dst + ((chunk ^ (row & 7u)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
-                      v[4 * j + 3]);
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t chunk = static_cast<uint32_t>(local / 4 + j);
+            st_shared_v4(dst + ((chunk ^ (row & 7u)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                         v[4 * j + 3]);
+          }
         }
       }
-    }
-    cluster_sync();  // every slice has arrived
-    // ---- reduce locally in split order and store FP16 C ----
-    const int chunks = cols / 4;
-    int pm, pn;
-    grouped_tile(pair, args.tiles_m, args.tiles_n, args.group_m, pm, pn);
-    const int row_base = pm * 256 + static_cast<int>(rank) * 128;
-    const int col_base = pn * BN + split * cols;
-    const bool vec = (split_args.ldc % 4 == 0) &&
-                     ((reinterpret_cast<uintptr_t>(split_args.c) & 7) == 0);
-    for (int i = threadIdx.x; i < 128 * chunks; i += blockDim.x) {
-      const uint32_t row = static_cast<uint32_t>(i / chunks);
-      const uint32_t chunk = static_cast<uint32_t>(i % chunks);
-      const uint32_t offset = row * row_bytes + ((chunk ^ (row & 7u)) << 4);
-      float4 acc = ld_shared_f32x4(base + offset);
-      for (int s2 = 1; s2 < splits; ++s2) {
-        const float4 v = ld_shared_f32x4(base + s2 * slot_bytes + offset);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
-      }
-      const int m = row_base + static_cast<int>(row);
-      const int n = col_base + static_cast<int>(chunk) * 4;
-      if (m < args.m) {
-        __half* dst = split_args.c + static_cast<int64_t>(m) * split_args.ldc + n;
-        if (vec && n + 3 < args.n) {
-          __half2 lo = __floats2half2_rn(acc.x, acc.y);
-          __half2 hi = __floats2half2_rn(acc.z, acc.w);
-          uint2 packed;
-          packed.x = *reinterpret_cast<uint32_t*>(&lo);
-          packed.y = *reinterpret_cast<uint32_t*>(&hi);
-          *reinterpret_cast<uint2*>(dst) = packed;
-        } else {
-          const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
-          for (int j = 0; j < 4 && n + j < args.n; ++j) dst[j] = __float2half_rn(vals[j]);
+      fence_proxy_async_smem();
+      named_barrier(1, 128);
+      if (warp == 2 && lane == 0) {
+        for (int owner = 0; owner < splits; ++owner) {
+          if (owner == split) continue;
+          const uint32_t owner_rank = rank + 2u * static_cast<uint32_t>(owner);
+          bulk_copy_to_cluster(map_to_rank(smem_addr(incoming + slot_of(split, owner) * slice_bytes), owner_rank),
+                               outgoing + slot(owner) * slice_bytes, static_cast<uint32_t>(slice_bytes),
+                               map_to_rank(smem_addr(recv_bar), owner_rank));
         }
+      }
+      // ---- wait for the S - 1 slices this CTA owns the sum of ----
+      const bool arrived = __all_sync(0xffffffffu, mbar_wait(recv_bar, 0, abort_flag));
+      if (!arrived && lane == 0) raise_abort(args.status, abort_flag, kStatusEpilogueTimeout);
+      if (split_ready && arrived) {
+        int pm, pn;
+        grouped_tile(pair, args.tiles_m, args.tiles_n, args.group_m, pm, pn);
+        const int row0 = pm * 256 + static_cast<int>(rank) * 128 + quarter * 32;
+        uint8_t* staging = epi + (warp - 2) * 2 * kEpilogueStageBytes;
+        int buf = 0;
+#pragma unroll 1
+        for (int c = 0; c < cols; c += 64) {
+          uint32_t own[64];
+          tmem_ld_32x32b_x32(lane_tmem + split * cols + c, *reinterpret_cast<uint32_t(*)[32]>(own));
+          tmem_ld_32x32b_x32(lane_tmem + split * cols + c + 32, *reinterpret_cast<uint32_t(*)[32]>(own + 32));
+          tmem_ld_wait();
+          float acc[64];
+#pragma unroll
+          for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+          for (int src = 0; src < splits; ++src) {  // split order
+            if (src == split) {
+#pragma unroll
+              for (int j = 0; j < 64; ++j) acc[j] = src == 0 ? __uint_as_float(own[j]) : acc[j] + __uint_as_float(own[j]);
+            } else {
+              const uint32_t base_addr = smem_addr(incoming + slot(src) * slice_bytes) + row * row_bytes;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const uint32_t chunk = static_cast<uint32_t>(c / 4 + j);
+                const float4 v = ld_shared_f32x4(base_addr + ((chunk ^ (row & 7u)) << 4));
+                if (src == 0) {
+                  acc[4 * j] = v.x; acc[4 * j + 1] = v.y; acc[4 * j + 2] = v.z; acc[4 * j + 3] = v.w;
+                } else {
+                  acc[4 * j] += v.x; acc[4 * j + 1] += v.y; acc[4 * j + 2] += v.z; acc[4 * j + 3] += v.w;
+                }
+              }
+            }
+          }
+          uint8_t* dst = staging + buf * kEpilogueStageBytes;
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+          const uint32_t row_addr = smem_addr(dst) + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), pack_half2(acc[8 * j], acc[8 * j + 1]),
+                         pack_half2(acc[8 * j + 2], acc[8 * j + 3]), pack_half2(acc[8 * j + 4], acc[8 * j + 5]),
+                         pack_half2(acc[8 * j + 6], acc[8 * j + 7]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&map_c, dst, pn * BN + split * cols + c, row0);
+            bulk_commit_group();
+          }
+          buf ^= 1;
+        }
+        if (lane == 0) bulk_wait_group<0>();
+        __syncwarp();
       }
     }
   }

@@ -294,6 +294,22 @@ __device__ __forceinline__ float4 ld_shared_f32x4(uint32_t addr) {
   return v;
 }
 
+// Asynchronous bulk copy of `bytes` (multiple of 16) from this CTA's shared memory into the
+// shared memory of a CTA of the cluster; completion is counted in bytes on that CTA's mbarrier.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, const void* src,
+                                                     uint32_t bytes, uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst_cluster),
+      "r"(smem_addr(src)), "r"(bytes), "r"(bar_cluster)
+      : "memory");
+}
+
+// Barrier among the `count` threads of named barrier `id` (the epilogue warps).
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // Whole-cluster execution barrier (all threads of all CTAs of the cluster). The warp is
 // reconverged first: the .aligned barrier needs every lane at the same instruction, and callers
 // reach it from role branches that only lane 0 of a warp entered.
