@@ -272,14 +272,12 @@ PAIR_CANDIDATES: tuple[ActionCandidate, ...] = _sorted(
         ActionCandidate(PairConfig(256, 256, 64, 4, 6, 4)),
     )
 )
-#: Split-K pair candidates, offered while a 256 x 256 tiling leaves most SM pairs idle.
-PAIR_SPLIT_CANDIDATES: tuple[ActionCandidate, ...] = _sorted(
-    (
-        ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8, 2)),
-        ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8, 4)),
-        ActionCandidate(PairConfig(256, 128, 64, 4, 8, 8, 2)),
-    )
-)
+#: Split-K pair candidates: a (2, S) cluster per tile. At most 33 clusters of four and 15 of eight
+#: CTAs are resident on a B200 at once, so split 2 is offered while the 256 x 256 tiles fit 33
+#: clusters and split 4 while they fit 15.
+PAIR_SPLIT2 = ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8, 2))
+PAIR_SPLIT4 = ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8, 4))
+PAIR_SPLIT_CANDIDATES: tuple[ActionCandidate, ...] = _sorted((PAIR_SPLIT2, PAIR_SPLIT4))
 
 
 def pair_candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:
@@ -287,9 +285,12 @@ def pair_candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:
     if workload.m < PAIR_M_MINIMUM:
         return ()
     tiles = -(-workload.m // 256) * -(-workload.n // 256)
-    if tiles <= 40:
-        return _sorted((*PAIR_CANDIDATES, *PAIR_SPLIT_CANDIDATES))
-    return PAIR_CANDIDATES
+    extra = ()
+    if tiles <= 33:
+        extra += (PAIR_SPLIT2,)
+    if tiles <= 15:
+        extra += (PAIR_SPLIT4,)
+    return _sorted((*PAIR_CANDIDATES, *extra))
 
 
 def b200_candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:

@@ -346,9 +346,11 @@ int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t 
       const int64_t k_blocks = cdiv(k, bk);
       int splits = cfg->split_k;
       if (splits == 0) {
-        // Split K only while the tiles leave half the SM pairs idle.
+        // Split K while the tiles leave most SMs idle and a wave of (2, S) clusters holds them:
+        // a B200 keeps at most 33 clusters of four and 15 of eight CTAs resident.
         splits = 1;
-        while (splits < 4 && tiles * splits * 2 <= sms / 2) splits *= 2;
+        if (tiles * 4 <= sms && tiles <= 33) splits = 2;
+        if (tiles * 8 <= sms && tiles <= 15) splits = 4;
       }
       // Each CTA owns at least 64 columns (one TMA-store sub-tile) of the tile.
       while (splits > 1 && (bn / splits < 64 || splits > k_blocks ||
