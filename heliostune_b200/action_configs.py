@@ -351,21 +351,29 @@ def split_plan(k: int, block_k: int, splits: int) -> tuple[int, int]:
     return per_split, -(-k_blocks // per_split)
 
 
+def resident_clusters(size: int, sm_count: int) -> int:
+    """Clusters of ``size`` CTAs (one per SM) a B200 keeps resident at once.
+
+    ``cudaOccupancyMaxActiveClusters`` on the 148-SM B200 gives 148, 74, 33 and 15 for clusters
+    of 1, 2, 4 and 8 CTAs (the GPCs fit fewer large clusters); scaled to ``sm_count``.
+    """
+    per148 = {1: 148, 2: 74, 4: 33, 8: 15}[size]
+    return per148 * sm_count // 148
+
+
 def stream_splits(m: int, n: int, k: int, config: StreamConfig, sm_count: int) -> int:
     """The cluster size (K splits) a :class:`StreamConfig` launches with on ``sm_count`` SMs.
 
-    Automatic: the largest power of two <= 8 whose CTAs fit one wave. Then, as the launcher does,
-    halve until every split owns K blocks and all but the last the same number.
+    Automatic: the largest power of two <= 8 whose clusters are all resident in one wave. Then,
+    as the launcher does, halve until every split owns K blocks and all but the last the same
+    number.
     """
     k_blocks = -(-k // config.block_k)
     splits = config.split_k
     if splits == 0:
         n_tiles = -(-n // config.block_n)
-        slots = sm_count * stream_ctas_per_sm(
-            config.block_m, config.block_n, config.block_k, config.num_stages
-        )
         splits = 8
-        while splits > 1 and n_tiles * splits > slots:
+        while splits > 1 and n_tiles > resident_clusters(splits, sm_count):
             splits //= 2
     while splits > 1 and (splits > k_blocks or -(-k_blocks // -(-k_blocks // splits)) != splits):
         splits //= 2

@@ -284,6 +284,13 @@ int stream_ctas_per_sm(int mp, int nt, int bk, int stages) {
   return c < 1 ? 1 : c;
 }
 
+// Clusters of `size` CTAs (one CTA per SM) a B200 keeps resident at once: its GPCs fit 74 pairs,
+// 33 clusters of four and 15 of eight (cudaOccupancyMaxActiveClusters), scaled to `sms`.
+int64_t resident_clusters(int size, int sms) {
+  const int64_t per148 = size <= 1 ? 148 : size == 2 ? 74 : size <= 4 ? 33 : 15;
+  return per148 * sms / 148;
+}
+
 int stream_cluster_ctas_per_sm(int mp, int nt, int bk, int stages) {
   const int ring = stages * (nt + mp) * bk * 2;
   const int partial = nt * mp * 4;
@@ -349,8 +356,8 @@ int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t 
         // Split K while the tiles leave most SMs idle and a wave of (2, S) clusters holds them:
         // a B200 keeps at most 33 clusters of four and 15 of eight CTAs resident.
         splits = 1;
-        if (tiles * 4 <= sms && tiles <= 33) splits = 2;
-        if (tiles * 8 <= sms && tiles <= 15) splits = 4;
+        if (tiles * 4 <= sms && tiles <= resident_clusters(4, sms)) splits = 2;
+        if (tiles * 8 <= sms && tiles <= resident_clusters(8, sms)) splits = 4;
       }
       // Each CTA owns at least 64 columns (one TMA-store sub-tile) of the tile.
       while (splits > 1 && (bn / splits < 64 || splits > k_blocks ||
@@ -393,11 +400,10 @@ int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t 
       const int64_t k_blocks = cdiv(k, bk);
       int splits = cfg->split_k;
       if (splits == 0) {
-        // Largest power of two <= 8 whose CTAs still fit one wave of the SMs.
+        // Largest power of two <= 8 whose clusters are all resident in one wave.
         const int64_t n_tiles = cdiv(n, bn);
-        const int64_t slots = int64_t(sms) * stream_cluster_ctas_per_sm(p->mp, p->nt, p->bk, p->stages);
         splits = 8;
-        while (splits > 1 && n_tiles * splits > slots) splits /= 2;
+        while (splits > 1 && n_tiles > resident_clusters(splits, sms)) splits /= 2;
       }
       // Every split must own at least one K block and all splits the same count but the last.
       while (splits > 1 && (splits > k_blocks || cdiv(k_blocks, cdiv(k_blocks, splits)) != splits))

@@ -166,12 +166,13 @@ def test_stream_family() -> None:
         StreamConfig(16, 256, 64, 4, 8, 0)
     with pytest.raises(SchemaError):
         StreamConfig(16, 128, 64, 4, 8, 3)
-    # The automatic split is the largest power of two <= 8 that keeps one wave of CTAs.
-    one_per_sm = StreamConfig(16, 128, 64, 4, 8, 0)  # 146 KB of shared memory
-    assert stream_splits(1, 3584, 18944, one_per_sm, 148) == 4  # 28 tiles x 4 = 112 CTAs
-    two_per_sm = StreamConfig(16, 128, 64, 4, 6, 0)
-    assert stream_splits(1, 3584, 18944, two_per_sm, 148) == 8  # 224 CTAs on 296 slots
-    assert stream_splits(1, 37888, 3584, one_per_sm, 148) == 1  # 296 tiles already fill the GPU
+    # The automatic split is the largest power of two <= 8 whose clusters are all resident
+    # (148 / 74 / 33 / 15 clusters of 1 / 2 / 4 / 8 CTAs on a B200).
+    config = StreamConfig(16, 128, 64, 4, 8, 0)
+    assert stream_splits(1, 3584, 18944, config, 148) == 4  # 28 tiles: 28 clusters of four
+    assert stream_splits(1, 1024, 18944, config, 148) == 8  # 8 tiles: 8 clusters of eight
+    assert stream_splits(1, 37888, 3584, config, 148) == 1  # 296 tiles already fill the GPU
+    assert stream_splits(1, 8192, 4096, config, 148) == 2  # 64 tiles: 64 pairs
     # every split owns K blocks: K = 100 is two blocks of 64
     assert stream_splits(1, 256, 100, StreamConfig(16, 128, 64, 4, 8, 8), 148) == 2
 
