@@ -218,10 +218,10 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
     t0 = time.perf_counter()
     chosen = {}
     if args.force:
-        from heliostune_b200.action_configs import PAIR_SPLIT_CANDIDATES
+        from heliostune_b200.action_configs import PAIR_SPLIT_CANDIDATES, PAIR_STREAM_K_CANDIDATE
 
         for w in workloads:
-            by_key = {c.key: c for c in (*b200_candidates_for(w), *PAIR_SPLIT_CANDIDATES)}
+            by_key = {c.key: c for c in (*b200_candidates_for(w), *PAIR_SPLIT_CANDIDATES, PAIR_STREAM_K_CANDIDATE)}
             chosen[w.key] = by_key[args.force]
         from heliostune_b200.tuner import ProbeResult
 

@@ -63,6 +63,7 @@ EXPORTED_SYMBOLS = (
     "hst_ipc_export",
     "hst_ipc_import",
     "hst_ipc_close",
+    "hst_pair_stream_k_tiles",
 )
 
 
@@ -137,6 +138,7 @@ def _declare(lib: ctypes.CDLL) -> None:
                           _ptr, _size, _ptr],
             ctypes.c_int,
         ),
+        "hst_pair_stream_k_tiles": ([_i64, _i64, _i64, ctypes.POINTER(_i64)], ctypes.c_int),
         "hst_matmul_pair": (
             [_i32] * 5 + [_ptr, _i64, _i64, _ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i64,
                           _ptr, _size, _ptr],

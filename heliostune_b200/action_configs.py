@@ -125,6 +125,10 @@ class StreamConfig:
         return asdict(self)
 
 
+#: ``PairConfig.split_k`` value selecting the stream-K schedule (HST_PAIR_STREAM_K in the C ABI).
+PAIR_STREAM_K = -1
+
+
 @dataclass(frozen=True, slots=True)
 class PairConfig:
     """B200 CTA-pair GEMM (no reference counterpart): 256 x ``block_n`` tiles per two SMs.
@@ -135,7 +139,10 @@ class PairConfig:
     with two TMEM accumulators; ``num_stages`` is the ring depth per CTA. ``num_warps`` is kept
     for the key (the CTA runs six warps). ``split_k`` 2 or 4 (0 = automatic, only when the tiles
     would leave most SMs idle) lets 2 x ``split_k`` CTAs share one tile and sum their FP32
-    partials in split order through distributed shared memory.
+    partials in split order through distributed shared memory. ``split_k`` -1
+    (:data:`PAIR_STREAM_K`) balances a part-filled last wave by stream-K: the tiles
+    :func:`pair_stream_k_tiles` names are cut along K into one equal run of K blocks per pair,
+    whose pieces meet through FP32 partial tiles in the workspace.
     """
 
     block_m: int
@@ -157,13 +164,13 @@ class PairConfig:
             raise SchemaError("block_k must be 64 or 128")
         if self.num_warps not in (1, 2, 4, 8):
             raise SchemaError("num_warps must be one of 1, 2, 4, or 8")
-        exact_int(self.split_k, context="pair config split_k", minimum=0)
-        if self.split_k not in (0, 1, 2, 4):
-            raise SchemaError("split_k must be 0 (automatic), 1, 2 or 4")
+        exact_int(self.split_k, context="pair config split_k", minimum=PAIR_STREAM_K)
+        if self.split_k not in (PAIR_STREAM_K, 0, 1, 2, 4):
+            raise SchemaError("split_k must be -1 (stream-K), 0 (automatic), 1, 2 or 4")
 
     @property
     def key(self) -> str:
-        split = "" if self.split_k == 1 else f"-split{'auto' if self.split_k == 0 else self.split_k}"
+        split = {1: "", 0: "-splitauto", PAIR_STREAM_K: "-streamk"}.get(self.split_k, f"-split{self.split_k}")
         return (
             f"pair-m{self.block_m}n{self.block_n}k{self.block_k}"
             f"-w{self.num_warps}s{self.num_stages}g{self.group_m}{split}"
@@ -280,7 +287,29 @@ PAIR_SPLIT4 = ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8, 4))
 PAIR_SPLIT_CANDIDATES: tuple[ActionCandidate, ...] = _sorted((PAIR_SPLIT2, PAIR_SPLIT4))
 
 
-def pair_candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:
+#: Stream-K pair candidate, offered where the 256 x 256 tiles leave the last wave of pairs
+#: part-filled (see :func:`pair_stream_k_tiles`).
+PAIR_STREAM_K_CANDIDATE = ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8, PAIR_STREAM_K))
+
+
+def pair_stream_k_tiles(tiles: int, k_blocks: int, pairs: int) -> int:
+    """Tiles the stream-K pair schedule shares out along K over ``pairs`` persistent pairs.
+
+    None when the tiles fill whole waves; all of them below one wave; otherwise the part-filled
+    last wave, plus one full wave when the last wave holds under a quarter of the pairs (so no
+    tile is cut into more than about five pieces); none when a pair would get under two of the
+    shared K blocks. The native planner applies the same rule (``hst_pair_stream_k_tiles``).
+    """
+    if tiles <= 0 or k_blocks <= 0 or pairs <= 0:
+        return 0
+    waves, rest = divmod(tiles, pairs)
+    if rest == 0:
+        return 0
+    shared = tiles if waves == 0 else (rest if rest * 4 >= pairs else rest + pairs)
+    return shared if shared * k_blocks >= 2 * pairs else 0
+
+
+def pair_candidates_for(workload: Workload, sm_count: int = 148) -> tuple[ActionCandidate, ...]:
     """B200 CTA-pair candidates for ``M > 128`` (empty below)."""
     if workload.m < PAIR_M_MINIMUM:
         return ()
@@ -290,6 +319,8 @@ def pair_candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:
         extra += (PAIR_SPLIT2,)
     if tiles <= 15:
         extra += (PAIR_SPLIT4,)
+    if pair_stream_k_tiles(tiles, -(-workload.k // 64), resident_clusters(2, sm_count)) > 0:
+        extra += (PAIR_STREAM_K_CANDIDATE,)
     return _sorted((*PAIR_CANDIDATES, *extra))
 
 

@@ -5,9 +5,11 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <chrono>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
+#include <random>
 #include <cstring>
 #include <string>
 
@@ -261,11 +263,33 @@ struct Plan {
   int um, ma, bn, bk, stages, group_m;
   // split-K / stream
   int nt, mp, splits, kb_per_split;
+  // pair stream-K: tiles shared out along K, pairs launched
+  int sk_tiles, sk_pairs;
   // workspace offsets (bytes) and sizes
   bool pack_a, pack_b, c_tmp;
   int64_t lda_p, ldb_p, ldc_p;
-  size_t off_a, off_b, off_c, off_p, total;
+  size_t off_a, off_b, off_c, off_p, off_sk, total;
 };
+
+// Tiles of a pair GEMM to share out along K (stream-K) over `pairs` persistent pairs: none when
+// the tiles fill whole waves; all of them when there is less than one wave; otherwise the
+// part-filled last wave, together with one full wave when the last wave holds under a quarter
+// of the pairs (so that no tile is cut into more than about five pieces). Zero as well when the
+// shared K blocks would give a pair fewer than two.
+// Stream-K workspace: one 256 x bn FP32 partial tile per pair, then 8 publication words per pair.
+size_t pair_partials_bytes(int pairs, int bn) { return size_t(pairs) * 256 * bn * 4; }
+size_t pair_stream_k_bytes(int pairs, int bn) {
+  return pair_partials_bytes(pairs, bn) + size_t(pairs) * 8 * sizeof(unsigned long long);
+}
+
+int64_t pair_stream_k_tiles(int64_t tiles, int64_t k_blocks, int64_t pairs) {
+  if (tiles <= 0 || k_blocks <= 0 || pairs <= 0) return 0;
+  const int64_t waves = tiles / pairs, rest = tiles % pairs;
+  if (rest == 0) return 0;
+  int64_t sk = waves == 0 ? tiles : (rest * 4 >= pairs ? rest : rest + pairs);
+  if (sk * k_blocks < 2 * pairs) sk = 0;
+  return sk;
+}
 
 int split_plan(int64_t k, int bk, int requested, int* kb_per_split, int* splits) {
   const int64_t k_blocks = cdiv(k, bk);
@@ -341,8 +365,8 @@ int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t 
       if (bm != 256) return fail(HST_ERR_UNSUPPORTED, "pair tiles have block_m 256");
       if (bn != 128 && bn != 256) return fail(HST_ERR_UNSUPPORTED, "pair block_n must be 128 or 256");
       if (bk != 64 && bk != 128) return fail(HST_ERR_UNSUPPORTED, "pair block_k must be 64 or 128");
-      if (cfg->split_k < 0 || cfg->split_k > 4 || cfg->split_k == 3)
-        return fail(HST_ERR_INVALID, "pair split_k must be 0 (automatic), 1, 2 or 4");
+      if (cfg->split_k < HST_PAIR_STREAM_K || cfg->split_k > 4 || cfg->split_k == 3)
+        return fail(HST_ERR_INVALID, "pair split_k must be -1 (stream-K), 0 (automatic), 1, 2 or 4");
       p->um = 128;
       p->ma = 2;
       p->bn = bn;
@@ -351,6 +375,15 @@ int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t 
       p->group_m = cfg->group_m;
       const int64_t tiles = cdiv(m, 256) * cdiv(n, bn);
       const int64_t k_blocks = cdiv(k, bk);
+      const int64_t max_pairs = sms / 2;
+      p->sk_pairs = static_cast<int>(tiles < max_pairs ? tiles : max_pairs);
+      if (cfg->split_k == HST_PAIR_STREAM_K) {
+        p->splits = 1;
+        p->kb_per_split = static_cast<int>(k_blocks);
+        p->sk_tiles = static_cast<int>(pair_stream_k_tiles(tiles, k_blocks, max_pairs));
+        if (p->sk_tiles > 0) p->sk_pairs = static_cast<int>(max_pairs);
+        break;
+      }
       int splits = cfg->split_k;
       if (splits == 0) {
         // Split K while the tiles leave most SMs idle and a wave of (2, S) clusters holds them:
@@ -433,6 +466,9 @@ int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t 
   p->off_p = off;
   if (p->family == HST_FAMILY_SPLIT_K && p->splits > 1)
     off = align_up(off + size_t(p->splits) * m * n * 4);
+  p->off_sk = off;
+  if (p->family == HST_FAMILY_PAIR && p->sk_tiles > 0)
+    off = align_up(off + pair_stream_k_bytes(p->sk_pairs, p->bn));
   p->total = off;
   return HST_OK;
 }
@@ -518,7 +554,8 @@ int dispatch_tile(const DeviceState& dev, const Plan& p, const Operands& o, bool
 
 template <int BN, int BK, bool SPLIT>
 int launch_pair(const DeviceState& dev, const Operands& o, int stages, int group_m, int splits,
-                int kb_per_split, cudaStream_t stream, const PairFanoutArgs* fanout_in = nullptr) {
+                int kb_per_split, cudaStream_t stream, const PairFanoutArgs* fanout_in = nullptr,
+                const PairStreamKArgs* sk_in = nullptr, int sk_pairs = 0) {
   using S = PairShape<BN, BK>;
   static std::atomic<uint64_t> smem_done{0};
   HST_TRY(allow_smem(pair_gemm_kernel<BN, BK, SPLIT>, smem_done));
@@ -552,8 +589,10 @@ int launch_pair(const DeviceState& dev, const Operands& o, int stages, int group
   split_args.kb_per_split = kb_per_split;
   split_args.c = o.c;
   split_args.ldc = o.ldc;
+  PairStreamKArgs sk = {};
+  if (sk_in != nullptr) sk = *sk_in;
   const int max_pairs = dev.sm_count / 2;
-  const int pairs = args.num_tiles < max_pairs ? args.num_tiles : max_pairs;
+  const int pairs = sk.sk_tiles > 0 ? sk_pairs : (args.num_tiles < max_pairs ? args.num_tiles : max_pairs);
   cudaLaunchConfig_t lc = {};
   lc.gridDim = SPLIT ? dim3(static_cast<unsigned>(2 * args.num_tiles), static_cast<unsigned>(splits))
                      : dim3(static_cast<unsigned>(2 * pairs));
@@ -568,17 +607,41 @@ int launch_pair(const DeviceState& dev, const Operands& o, int stages, int group
   lc.attrs = attr;
   lc.numAttrs = 1;
   HST_CUDA(cudaLaunchKernelEx(&lc, pair_gemm_kernel<BN, BK, SPLIT>, ma_, mb_, mc_, args, split_args,
-                              fanout));
+                              fanout, sk));
   return HST_OK;
 }
 
-int dispatch_pair(const DeviceState& dev, const Plan& p, const Operands& o, cudaStream_t stream) {
+// Publication value of a stream-K launch: unique per launch within the process, and started
+// from a per-process random value so that words left in reused memory by another process (or
+// any other data) match with probability ~2^-64.
+unsigned long long next_stream_k_token() {
+  static std::atomic<unsigned long long> counter{0};
+  static const unsigned long long base = [] {
+    std::random_device rd;
+    return (static_cast<unsigned long long>(rd()) << 32) ^ rd() ^
+           static_cast<unsigned long long>(std::chrono::steady_clock::now().time_since_epoch().count());
+  }();
+  unsigned long long t = 0;
+  while (t == 0) t = base + counter.fetch_add(1, std::memory_order_relaxed);
+  return t;
+}
+
+int dispatch_pair(const DeviceState& dev, const Plan& p, const Operands& o, uint8_t* ws,
+                  cudaStream_t stream) {
+  PairStreamKArgs sk = {};
+  if (p.sk_tiles > 0) {
+    sk.sk_tiles = p.sk_tiles;
+    sk.partials = reinterpret_cast<float*>(ws + p.off_sk);
+    sk.flags = reinterpret_cast<unsigned long long*>(ws + p.off_sk + pair_partials_bytes(p.sk_pairs, p.bn));
+    sk.token = next_stream_k_token();
+  }
 #define HST_PAIR_CASE(BN_, BK_)                                                                \
   if (p.bn == BN_ && p.bk == BK_) {                                                            \
     if (p.splits > 1)                                                                          \
       return launch_pair<BN_, BK_, true>(dev, o, p.stages, p.group_m, p.splits, p.kb_per_split, \
                                          stream);                                              \
-    return launch_pair<BN_, BK_, false>(dev, o, p.stages, p.group_m, 1, 0, stream);            \
+    return launch_pair<BN_, BK_, false>(dev, o, p.stages, p.group_m, 1, 0, stream, nullptr,    \
+                                        &sk, p.sk_pairs);                                      \
   }
   HST_PAIR_CASE(256, 64)
   HST_PAIR_CASE(128, 64)
@@ -821,7 +884,7 @@ int gemm_impl(const hst_gemm_config* cfg, const void* a, int64_t sa0, int64_t sa
     o.ldc = p.ldc_p;
   }
   if (p.family == HST_FAMILY_PAIR) {
-    HST_TRY(dispatch_pair(*dev, p, o, stream));
+    HST_TRY(dispatch_pair(*dev, p, o, ws, stream));
   } else {
     HST_TRY(dispatch_tile(*dev, p, o, p.family == HST_FAMILY_PERSISTENT, stream));
   }
@@ -851,6 +914,14 @@ const char* hst_last_error(void) { return t_error.c_str(); }
 int hst_device_sm_count(int device, int* sm_count) {
   if (sm_count == nullptr) return fail(HST_ERR_INVALID, "sm_count is null");
   HST_CUDA(cudaDeviceGetAttribute(sm_count, cudaDevAttrMultiProcessorCount, device));
+  return HST_OK;
+}
+
+int hst_pair_stream_k_tiles(int64_t tiles, int64_t k_blocks, int64_t pairs, int64_t* sk_tiles) {
+  if (sk_tiles == nullptr) return fail(HST_ERR_INVALID, "sk_tiles is null");
+  if (tiles < 0 || k_blocks < 0 || pairs < 1)
+    return fail(HST_ERR_INVALID, "tiles and k_blocks must be >= 0 and pairs >= 1");
+  *sk_tiles = pair_stream_k_tiles(tiles, k_blocks, pairs);
   return HST_OK;
 }
 

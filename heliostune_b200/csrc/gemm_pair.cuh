@@ -24,6 +24,17 @@
 // own slice read straight from TMEM and the S - 1 received slices, and stores FP16 C through
 // the usual staged TMA-store epilogue. One tile per cluster; no workspace, no atomics, bitwise
 // reproducible.
+//
+// Stream-K (persistent mode with PairStreamKArgs::sk_tiles > 0), for tile counts that leave the
+// last wave of pairs part-empty: the first sk_tiles tiles are cut along K into one contiguous
+// range of (tile, K block) iterations per pair, so every pair does the same number of K
+// blocks; the remaining tiles follow round-robin as whole tiles. A piece that does not start at
+// the tile's first K block is published as an FP32 partial tile in global memory (one slot per
+// pair, 16-byte chunks laid out so a warp's 32 rows are one 512-byte run) with a release flag
+// per epilogue warp. The piece holding the tile's first K blocks belongs to the highest-numbered
+// pair among the tile's pieces and is the last of that pair's stream-K work; its epilogue waits
+// for the flags, adds the partials in K order onto its accumulator and stores FP16 C. Finishers
+// only ever wait on lower-numbered pairs, which never wait on them. Bitwise reproducible.
 // No TMA load here feeds more than one CTA's shared memory.
 #pragma once
 
@@ -71,12 +82,63 @@ struct PairSplitArgs {
   int64_t ldc;
 };
 
+struct PairStreamKArgs {
+  int sk_tiles;               // tiles [0, sk_tiles) are shared out along K (0 = whole tiles only)
+  float* partials;            // [pairs][2 CTAs][BN / 4 chunks][128 rows][4] FP32, one tile per pair
+  unsigned long long* flags;  // [pairs][2 CTAs][4 epilogue warps] publication words
+  unsigned long long token;   // the value that publishes a partial in this launch
+};
+
+// The work of one pair in order, as segments (tile, [kb0, kb1)): first its share of the
+// stream-K iterations (tile-major, K-block-minor over tiles [0, sk_tiles); pair p takes share
+// pairs - 1 - p), then whole tiles sk_tiles + p, sk_tiles + p + pairs, ...
+struct PairWork {
+  int64_t total;  // stream-K iterations of all pairs
+  int64_t it, hi;
+  int pairs, next_tile, num_tiles, k_blocks;
+
+  __device__ static int64_t share_begin(int64_t total, int pairs, int pair) {
+    return total * (pairs - 1 - pair) / pairs;
+  }
+  __device__ static int64_t share_end(int64_t total, int pairs, int pair) {
+    return total * (pairs - pair) / pairs;
+  }
+  __device__ PairWork(const TileArgs& a, int sk_tiles, int pair, int pairs_)
+      : total(int64_t(sk_tiles) * a.k_blocks),
+        pairs(pairs_),
+        next_tile(sk_tiles + pair),
+        num_tiles(a.num_tiles),
+        k_blocks(a.k_blocks) {
+    it = share_begin(total, pairs, pair);
+    hi = share_end(total, pairs, pair);
+  }
+  __device__ bool next(int& tile, int& kb0, int& kb1) {
+    if (it < hi) {
+      tile = static_cast<int>(it / k_blocks);
+      kb0 = static_cast<int>(it - int64_t(tile) * k_blocks);
+      const int64_t left = hi - it;
+      kb1 = left < int64_t(k_blocks - kb0) ? kb0 + static_cast<int>(left) : k_blocks;
+      it += kb1 - kb0;
+      return true;
+    }
+    if (next_tile < num_tiles) {
+      tile = next_tile;
+      kb0 = 0;
+      kb1 = k_blocks;
+      next_tile += pairs;
+      return true;
+    }
+    return false;
+  }
+};
+
 template <int BN, int BK, bool SPLIT>
 __global__ void __launch_bounds__(kTileThreads, 1)
     pair_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                      const __grid_constant__ CUtensorMap map_b,
                      const __grid_constant__ CUtensorMap map_c, const TileArgs args,
-                     const PairSplitArgs split_args, const __grid_constant__ PairFanoutArgs fanout) {
+                     const PairSplitArgs split_args, const __grid_constant__ PairFanoutArgs fanout,
+                     const PairStreamKArgs sk) {
   using S = PairShape<BN, BK>;
 
   extern __shared__ uint8_t smem_raw[];
@@ -105,6 +167,16 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   const int split = SPLIT ? static_cast<int>(blockIdx.y) : 0;
   const int kb_begin = SPLIT ? split * split_args.kb_per_split : 0;
   const int kb_end = SPLIT ? min(kb_begin + split_args.kb_per_split, args.k_blocks) : args.k_blocks;
+  const int sk_tiles = SPLIT ? 0 : sk.sk_tiles;
+  // One segment of this pair's work: split mode has one tile and this split's K blocks.
+  auto next_segment = [&](PairWork& work, int& tile, int& kb0, int& kb1) {
+    if (!work.next(tile, kb0, kb1)) return false;
+    if (SPLIT) {
+      kb0 = kb_begin;
+      kb1 = kb_end;
+    }
+    return true;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -145,12 +217,14 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     uint32_t phase = 0;
     uint32_t armed_mask = 0, armed_parity = 0;
     bool ok = true;
-    for (int tile = pair; tile < args.num_tiles && ok; tile += pairs) {
+    PairWork work(args, sk_tiles, pair, pairs);
+    int tile, kb0, kb1;
+    while (ok && next_segment(work, tile, kb0, kb1)) {
       int pm, pn;
       grouped_tile(tile, args.tiles_m, args.tiles_n, args.group_m, pm, pn);
       const int m0 = pm * 256 + static_cast<int>(rank) * 128;
       const int n0 = pn * BN + static_cast<int>(rank) * S::kHalfN;
-      for (int kb = kb_begin; kb < kb_end; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
           raise_abort(args.status, abort_flag, kStatusProducerTimeout);
           ok = false;
@@ -194,7 +268,9 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int tile = pair; tile < args.num_tiles && ok; tile += pairs) {
+    PairWork work(args, sk_tiles, pair, pairs);
+    int tile, kb0, kb1;
+    while (ok && next_segment(work, tile, kb0, kb1)) {
       if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort_flag)) {
         raise_abort(args.status, abort_flag, kStatusMmaTimeout);
         ok = false;
@@ -202,7 +278,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       }
       tc_fence_after_sync();
       const uint32_t d_base = tmem_base + acc * S::kAccCols;
-      for (int kb = kb_begin; kb < kb_end; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&full[stage], phase, abort_flag)) {
           raise_abort(args.status, abort_flag, kStatusMmaTimeout);
           ok = false;
@@ -216,7 +292,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           const uint64_t adesc =
               smem_desc(a_base + (kk >> 2) * S::kABoxBytes + (kk & 3) * 32, 16, 1024);
           const uint64_t bdesc = smem_desc(b_base + kk * 2048, S::kBBoxBytes, 1024);
-          umma_f16_pair(d_base, adesc, bdesc, S::kIdesc, (kb != kb_begin || kk != 0) ? 1u : 0u);
+          umma_f16_pair(d_base, adesc, bdesc, S::kIdesc, (kb != kb0 || kk != 0) ? 1u : 0u);
         }
         const uint32_t own_empty = smem_addr(&empty[stage]);
         umma_commit_pair(own_empty);
@@ -244,11 +320,20 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   } else if (!SPLIT && warp >= 2) {
     // ---------------- epilogue (both CTAs, own 128 rows) ----------------
     const int quarter = warp & 3;
+    const int row = quarter * 32 + static_cast<int>(lane);  // row of this CTA's 128
     uint8_t* staging = epi + (warp - 2) * 2 * kEpilogueStageBytes;
     int buf = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = pair; tile < args.num_tiles; tile += pairs) {
+    constexpr int kChunks = BN / 4;  // 16-byte chunks of one partial-tile row
+    // Partial-tile slot of pair q for this CTA, and its publication word for this warp.
+    auto slot_of_pair = [&](int q) {
+      return sk.partials + (static_cast<size_t>(q) * 2 + rank) * (kChunks * 128 * 4);
+    };
+    auto flag_of_pair = [&](int q) { return sk.flags + (static_cast<size_t>(q) * 2 + rank) * 4 + quarter; };
+    PairWork work(args, sk_tiles, pair, pairs);
+    int tile, kb0, kb1;
+    while (next_segment(work, tile, kb0, kb1)) {
       int pm, pn;
       grouped_tile(tile, args.tiles_m, args.tiles_n, args.group_m, pm, pn);
       const int row0 = pm * 256 + static_cast<int>(rank) * 128 + quarter * 32;
@@ -259,56 +344,110 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         break;
       }
       tc_fence_after_sync();
+      const uint32_t lane_tmem = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * S::kAccCols;
+      const int64_t tile_end = int64_t(tile + 1) * args.k_blocks;  // stream-K iteration after the tile
+      if (kb0 > 0) {
+        // ---- a later K range of a shared tile: publish it as an FP32 partial ----
+        float* slot = slot_of_pair(pair);
 #pragma unroll 1
-      for (int c = 0; c < BN / 64; ++c) {
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                               acc * S::kAccCols + c * 64;
-        uint32_t lo[32], hi[32];
-        tmem_ld_32x32b_x32(taddr, lo);
-        tmem_ld_32x32b_x32(taddr + 32, hi);
-        tmem_ld_wait();
-        uint8_t* dst = staging + buf * kEpilogueStageBytes;
-        if (lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
-        const uint32_t row_addr = smem_addr(dst) + lane * 128;
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(lane_tmem + c, v);
+          tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t* src = (j < 4) ? &lo[j * 8] : &hi[(j - 4) * 8];
-          const uint32_t w0 = pack_half2(__uint_as_float(src[0]), __uint_as_float(src[1]));
-          const uint32_t w1 = pack_half2(__uint_as_float(src[2]), __uint_as_float(src[3]));
-          const uint32_t w2 = pack_half2(__uint_as_float(src[4]), __uint_as_float(src[5]));
-          const uint32_t w3 = pack_half2(__uint_as_float(src[6]), __uint_as_float(src[7]));
-          st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), w0, w1, w2, w3);
+          for (int j = 0; j < 8; ++j) {
+            st_global_v4(slot + (static_cast<size_t>(c / 4 + j) * 128 + row) * 4, v[4 * j], v[4 * j + 1],
+                         v[4 * j + 2], v[4 * j + 3]);
+          }
         }
-        fence_proxy_async_smem();
+        __threadfence();
         __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&map_c, dst, n0 + c * 64, row0);
-          bulk_commit_group();
+        if (lane == 0) st_release_gpu_u64(flag_of_pair(pair), sk.token);
+      } else {
+        // ---- a whole tile, or a shared tile's first K range: its finisher ----
+        const bool finisher = kb1 < args.k_blocks;
+        bool have = true;
+        if (finisher) {
+          // The tile's later K ranges belong to pairs pair - 1, pair - 2, ... (adjacent shares).
+          int64_t pos = work.it;  // first iteration after this pair's piece
+          for (int q = pair - 1; q >= 0 && pos < tile_end && have; --q) {
+            const int64_t end = PairWork::share_end(work.total, pairs, q);
+            if (end > pos && lane == 0) have = wait_flag_u64(flag_of_pair(q), sk.token, abort_flag);
+            pos = end > pos ? end : pos;
+          }
+          have = __all_sync(0xffffffffu, have);
+          if (!have && lane == 0) raise_abort(args.status, abort_flag, kStatusEpilogueTimeout);
         }
-        if (fanout.count > 0) {
-          // Each lane moves 8 of the sub-tile's 256 16-byte chunks; one shared-memory read per
-          // chunk feeds every peer. Rows and columns past the slice are skipped.
-          const uint32_t src = smem_addr(dst);
 #pragma unroll 1
-          for (int i = static_cast<int>(lane); i < 256; i += 32) {
-            const int r = i >> 3, ch = i & 7;
-            const int m = row0 + r, n = n0 + c * 64 + ch * 8;
-            if (m >= args.m || n >= args.n) continue;
-            const float4 v = ld_shared_f32x4(src + r * 128 + ((ch ^ (r & 7)) << 4));
-            const bool full8 = n + 8 <= args.n;
-            for (int q = 0; q < fanout.count; ++q) {
-              __half* out = reinterpret_cast<__half*>(fanout.peers[q]) + static_cast<int64_t>(m) * fanout.ldc + n;
-              if (full8) {
-                *reinterpret_cast<float4*>(out) = v;
-              } else {
-                const __half* h = reinterpret_cast<const __half*>(&v);
-                for (int j = 0; j < 8 && n + j < args.n; ++j) out[j] = h[j];
+        for (int c = 0; c < BN / 64 && have; ++c) {
+          const uint32_t taddr = lane_tmem + c * 64;
+          uint32_t lo[32], hi[32];
+          tmem_ld_32x32b_x32(taddr, lo);
+          tmem_ld_32x32b_x32(taddr + 32, hi);
+          tmem_ld_wait();
+          if (finisher) {
+            // Add the later K ranges in K order (pair - 1 first).
+            int64_t pos = work.it;
+            for (int q = pair - 1; q >= 0 && pos < tile_end; --q) {
+              const int64_t end = PairWork::share_end(work.total, pairs, q);
+              if (end > pos) {
+                const float* part = slot_of_pair(q) + (static_cast<size_t>(c * 16) * 128 + row) * 4;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const float4 p = ld_global_cg_f32x4(part + static_cast<size_t>(j) * 128 * 4);
+                  uint32_t* d = j < 8 ? &lo[4 * j] : &hi[4 * (j - 8)];
+                  d[0] = __float_as_uint(__uint_as_float(d[0]) + p.x);
+                  d[1] = __float_as_uint(__uint_as_float(d[1]) + p.y);
+                  d[2] = __float_as_uint(__uint_as_float(d[2]) + p.z);
+                  d[3] = __float_as_uint(__uint_as_float(d[3]) + p.w);
+                }
+                pos = end;
               }
             }
           }
+          uint8_t* dst = staging + buf * kEpilogueStageBytes;
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+          const uint32_t row_addr = smem_addr(dst) + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t* src = (j < 4) ? &lo[j * 8] : &hi[(j - 4) * 8];
+            const uint32_t w0 = pack_half2(__uint_as_float(src[0]), __uint_as_float(src[1]));
+            const uint32_t w1 = pack_half2(__uint_as_float(src[2]), __uint_as_float(src[3]));
+            const uint32_t w2 = pack_half2(__uint_as_float(src[4]), __uint_as_float(src[5]));
+            const uint32_t w3 = pack_half2(__uint_as_float(src[6]), __uint_as_float(src[7]));
+            st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), w0, w1, w2, w3);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&map_c, dst, n0 + c * 64, row0);
+            bulk_commit_group();
+          }
+          if (fanout.count > 0) {
+            // Each lane moves 8 of the sub-tile's 256 16-byte chunks; one shared-memory read per
+            // chunk feeds every peer. Rows and columns past the slice are skipped.
+            const uint32_t src = smem_addr(dst);
+#pragma unroll 1
+            for (int i = static_cast<int>(lane); i < 256; i += 32) {
+              const int r = i >> 3, ch = i & 7;
+              const int m = row0 + r, n = n0 + c * 64 + ch * 8;
+              if (m >= args.m || n >= args.n) continue;
+              const float4 v = ld_shared_f32x4(src + r * 128 + ((ch ^ (r & 7)) << 4));
+              const bool full8 = n + 8 <= args.n;
+              for (int q = 0; q < fanout.count; ++q) {
+                __half* out = reinterpret_cast<__half*>(fanout.peers[q]) + static_cast<int64_t>(m) * fanout.ldc + n;
+                if (full8) {
+                  *reinterpret_cast<float4*>(out) = v;
+                } else {
+                  const __half* h = reinterpret_cast<const __half*>(&v);
+                  for (int j = 0; j < 8 && n + j < args.n; ++j) out[j] = h[j];
+                }
+              }
+            }
+          }
+          buf ^= 1;
         }
-        buf ^= 1;
       }
       tc_fence_before_sync();
       __syncwarp();

@@ -305,6 +305,53 @@ __device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, const
       : "memory");
 }
 
+// ------------------------------------------------------------------------------------------
+// Global-memory hand-off between CTAs of one launch (stream-K partial tiles)
+// ------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ void st_release_gpu_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Waits until *flag holds `token`. Gives up after `limit_ns` or once `abort` is raised.
+__device__ __forceinline__ bool wait_flag_u64(const unsigned long long* flag,
+                                              unsigned long long token, volatile int* abort,
+                                              uint64_t limit_ns = kWaitLimitNs) {
+  if (ld_acquire_gpu_u64(flag) == token) return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i) {
+      if (ld_acquire_gpu_u64(flag) == token) return true;
+      __nanosleep(100);
+    }
+    if (abort != nullptr && *abort) return false;
+    if (global_timer_ns() - start > limit_ns) return false;
+  }
+}
+
+// 16-byte global load through L2 only (data another SM wrote during this launch).
+__device__ __forceinline__ float4 ld_global_cg_f32x4(const float* p) {
+  float4 v;
+  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_global_v4(float* p, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
 // Barrier among the `count` threads of named barrier `id` (the epilogue warps).
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

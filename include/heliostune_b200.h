@@ -42,6 +42,9 @@ extern "C" {
 #define HST_FAMILY_STREAM 3     /* StreamConfig        -> swap-AB weight streaming, M <= 256 */
 #define HST_FAMILY_PAIR 4       /* PairConfig          -> CTA-pair (cta_group::2) 256 x N tiles */
 
+/* split_k of the pair family that selects its stream-K schedule (no reference counterpart). */
+#define HST_PAIR_STREAM_K (-1)
+
 /* Field names and meaning follow the reference's config dataclasses
  * (configs.py:11-51, configs.py:269-356, action_configs.py:20-59). group_m is ignored by the
  * split-K and stream families; split_k by the tile and persistent families (0 = automatic for
@@ -115,12 +118,21 @@ int hst_matmul_stream(int32_t block_m, int32_t block_n, int32_t block_k, int32_t
 /* B200 CTA-pair family (no reference counterpart): clusters of two CTAs computing 256 x block_n
  * tiles (block_n 128 or 256) with tcgen05.mma.cta_group::2, persistent over the tiles. split_k
  * 2 or 4 (0 = automatic when the tiles leave most SMs idle) makes clusters of 2 x split_k CTAs
- * that divide K and sum their partials in split order through distributed shared memory. Any
- * strides (packed through the workspace when a TMA tensor map cannot describe them). */
+ * that divide K and sum their partials in split order through distributed shared memory.
+ * split_k HST_PAIR_STREAM_K balances a part-filled last wave: the tiles
+ * hst_pair_stream_k_tiles names are cut along K into one equal run of K blocks per pair, the
+ * rest stay whole; pieces meet through FP32 partial tiles and publication words in the
+ * workspace (hst_gemm_workspace_size covers them; no zeroing needed: each launch publishes a
+ * value of its own). Calls that share a workspace must not overlap on the GPU. Any strides
+ * (packed through the workspace when a TMA tensor map cannot describe them). */
 int hst_matmul_pair(int32_t block_n, int32_t block_k, int32_t num_stages, int32_t group_m,
                     int32_t split_k, const void* a, int64_t a_stride0, int64_t a_stride1, const void* b,
                     int64_t b_stride0, int64_t b_stride1, void* c, int64_t ldc, int64_t m,
                     int64_t n, int64_t k, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Host-only planning query of the stream-K schedule: how many of `tiles` pair tiles (each
+ * k_blocks K blocks deep) are shared out along K over `pairs` persistent pairs (0 = none). */
+int hst_pair_stream_k_tiles(int64_t tiles, int64_t k_blocks, int64_t pairs, int64_t* sk_tiles);
 
 /* y[r, :] = fp16((x[r, :] * rsqrt(mean(x[r, :]^2) + eps)) * gamma), FP32 row sum.
  * Replaces the residual RMSNorm op (_fusion_gpu.py:49-94) in the form measured here: FP16,

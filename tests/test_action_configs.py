@@ -19,6 +19,8 @@ from heliostune_b200.action_configs import (
     action_set_manifest,
     b200_candidates_for,
     candidates_for,
+    pair_candidates_for,
+    pair_stream_k_tiles,
     split_plan,
     stream_block_m,
     stream_candidates_for,
@@ -182,3 +184,67 @@ def test_split_plan_matches_the_reference_interval_rule() -> None:
     assert split_plan(1543, 64, 16) == (2, 13)
     assert split_plan(17, 64, 16) == (1, 1)
     assert split_plan(18944, 64, 4) == (74, 4)
+
+
+def _pair_work(tiles: int, k_blocks: int, pairs: int, sk_tiles: int, pair: int) -> list[tuple[int, int, int]]:
+    """Segments (tile, kb0, kb1) of one pair, in order, as the pair kernel's PairWork walks them."""
+    total = sk_tiles * k_blocks
+    it, hi = total * (pairs - 1 - pair) // pairs, total * (pairs - pair) // pairs
+    out = []
+    while it < hi:
+        tile, kb0 = divmod(it, k_blocks)
+        kb1 = min(k_blocks, kb0 + hi - it)
+        out.append((tile, kb0, kb1))
+        it += kb1 - kb0
+    out += [(t, 0, k_blocks) for t in range(sk_tiles + pair, tiles, pairs)]
+    return out
+
+
+@pytest.mark.parametrize(
+    ("tiles", "k_blocks"),
+    ((32, 64), (128, 64), (112, 56), (448, 296), (512, 224), (28, 296), (74, 64), (3, 5), (80, 2)),
+)
+def test_pair_stream_k_schedule_covers_every_k_block_once(tiles: int, k_blocks: int) -> None:
+    pairs = 74
+    sk = pair_stream_k_tiles(tiles, k_blocks, pairs)
+    launched = pairs if sk else min(tiles, pairs)
+    owners: dict[tuple[int, int], int] = {}
+    pieces: dict[int, list[tuple[int, int, int]]] = {}
+    work = [0] * launched
+    for pair in range(launched):
+        segs = _pair_work(tiles, k_blocks, launched, sk, pair)
+        for i, (tile, kb0, kb1) in enumerate(segs):
+            assert 0 <= kb0 < kb1 <= k_blocks
+            if kb0 > 0:
+                assert i == 0  # only a pair's first segment publishes a partial
+            if kb0 == 0 and kb1 < k_blocks:
+                # a finisher is the pair's last stream-K segment: whole tiles follow
+                assert tile < sk and all(t >= sk for t, _, _ in segs[i + 1 :])
+            for kb in range(kb0, kb1):
+                assert (tile, kb) not in owners
+                owners[(tile, kb)] = pair
+            pieces.setdefault(tile, []).append((kb0, kb1, pair))
+            work[pair] += kb1 - kb0
+    assert len(owners) == tiles * k_blocks
+    for tile, ps in pieces.items():
+        ps.sort()
+        if len(ps) > 1:
+            assert tile < sk
+            # the first K range is the finisher; the later ranges belong to ever lower pairs
+            assert [p for _, _, p in ps] == sorted((p for _, _, p in ps), reverse=True)
+            assert all(ps[i][1] == ps[i + 1][0] for i in range(len(ps) - 1))
+    if sk:
+        # stream-K balances the K blocks per pair to within one tile's depth
+        assert max(work) - min(work) <= k_blocks
+        assert max(len(ps) for ps in pieces.values()) <= max(2, -(-pairs // max(sk, 1)) + 1)
+
+
+def test_pair_stream_k_rule() -> None:
+    assert pair_stream_k_tiles(148, 64, 74) == 0  # whole waves
+    assert pair_stream_k_tiles(32, 64, 74) == 32  # under one wave: every tile
+    assert pair_stream_k_tiles(128, 64, 74) == 54  # the part-filled wave
+    assert pair_stream_k_tiles(448, 296, 74) == 78  # 4 left over: one full wave joins them
+    assert pair_stream_k_tiles(3, 5, 74) == 0  # under two K blocks per pair
+    w = Workload(2048, 4096, 4096, "x", "y", "z")
+    assert any(c.key.endswith("-streamk") for c in pair_candidates_for(w))
+    assert not any(c.key.endswith("-streamk") for c in pair_candidates_for(replace(w, m=8192, n=9472)))

@@ -17,6 +17,7 @@ from heliostune_b200 import _native
 from heliostune_b200.action_configs import (
     ALL_CANDIDATES,
     PAIR_CANDIDATES,
+    PAIR_STREAM_K,
     PairConfig,
     NON_SPLIT_CANDIDATES,
     SPLIT_K_CANDIDATES,
@@ -137,6 +138,67 @@ def test_pair_split_k(split: int, block_n: int, shape: tuple[int, int, int]) -> 
     assert torch.equal(first.view(torch.int16), launch(a, b, candidate).view(torch.int16))
 
 
+@pytest.mark.parametrize("block_n", (128, 256))
+@pytest.mark.parametrize(
+    "shape",
+    (
+        (512, 4096, 4096),  # under one wave: every tile shared along K
+        (2048, 3584, 3584),  # one full wave and a part-filled one
+        (8192, 3584, 640),  # four tiles past six waves: one full wave joins them
+        (512, 1024, 8192),  # few deep tiles: about ten pieces per tile
+        (600, 1000, 4000),  # ragged rows and columns
+        (300, 1032, 520),  # too little K to share: whole tiles only
+    ),
+    ids=lambda s: "x".join(map(str, s)),
+)
+def test_pair_stream_k(block_n: int, shape: tuple[int, int, int]) -> None:
+    m, n, k = shape
+    g = torch.Generator(device="cuda").manual_seed(m + n + block_n)
+    a = scaled_normal((m, k), k, g)
+    b = scaled_normal((k, n), k, g)
+    candidate = ActionCandidate(PairConfig(256, block_n, 64, 4, 6, 8, PAIR_STREAM_K))
+    first = launch(a, b, candidate)
+    assert_gemm_parity(first, a, b)
+    for _ in range(2):  # later launches see the earlier ones' publication words: never matched
+        assert torch.equal(first.view(torch.int16), launch(a, b, candidate).view(torch.int16))
+
+
+def test_pair_stream_k_ignores_stale_workspace_contents() -> None:
+    lib = _native.library()
+    m, n, k = 512, 4096, 2048
+    g = torch.Generator(device="cuda").manual_seed(77)
+    a = scaled_normal((m, k), k, g)
+    b = scaled_normal((k, n), k, g)
+    config = _native.GemmConfig(_native.FAMILY_PAIR, 256, 256, 64, 4, 6, 8, PAIR_STREAM_K)
+    size = ctypes.c_size_t()
+    _native.check(
+        lib.hst_gemm_workspace_size(
+            ctypes.byref(config), a.data_ptr(), k, 1, b.data_ptr(), n, 1, m, n, k,
+            torch.cuda.current_device(), ctypes.byref(size),
+        )
+    )
+    assert size.value >= 74 * 256 * 256 * 4  # one partial tile per pair
+    outputs = []
+    for fill in (0xFF, 0x00, None):
+        ws = torch.empty(size.value, dtype=torch.uint8, device="cuda")
+        if fill is None:
+            ws.random_(0, 256, generator=g)
+        else:
+            ws.fill_(fill)
+        for _ in range(2):  # the second call meets the first one's partials and words
+            c = torch.empty((m, n), dtype=torch.float16, device="cuda")
+            _native.check(
+                lib.hst_gemm(
+                    ctypes.byref(config), a.data_ptr(), k, 1, b.data_ptr(), n, 1, c.data_ptr(), n,
+                    m, n, k, ws.data_ptr(), size.value, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
+                )
+            )
+            outputs.append(c)
+    assert_gemm_parity(outputs[0], a, b)
+    for c in outputs[1:]:
+        assert torch.equal(outputs[0].view(torch.int16), c.view(torch.int16))
+
+
 def test_pair_family_with_strided_operands_and_deep_k() -> None:
     g = torch.Generator(device="cuda").manual_seed(9)
     a = scaled_normal((300, 2 * 1540), 1540, g)[:, ::2]
@@ -245,6 +307,7 @@ def test_full_size_grid_shapes(workload: Workload) -> None:
         ActionCandidate(StreamConfig(32, 128, 64, 4, 6, 8)),
         ActionCandidate(StreamConfig(128, 256, 64, 4, 3, 4)),
         ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8)),
+        ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8, PAIR_STREAM_K)),
     ],
     ids=lambda c: c.key,
 )

@@ -96,3 +96,15 @@ def test_missing_library_fails_loudly(monkeypatch: pytest.MonkeyPatch, tmp_path)
     monkeypatch.setattr(_native, "LIBRARY_PATH", tmp_path / "absent.so")
     with pytest.raises(_native.KernelError, match="not built"):
         _native.library()
+
+
+def test_stream_k_planning_matches_the_python_rule(lib: ctypes.CDLL) -> None:
+    from heliostune_b200.action_configs import pair_stream_k_tiles
+
+    out = ctypes.c_int64(-1)
+    for tiles in (0, 1, 3, 28, 32, 73, 74, 75, 112, 128, 148, 149, 448, 512, 576, 896, 1184):
+        for k_blocks in (1, 2, 5, 56, 64, 296):
+            for pairs in (1, 37, 74):
+                assert lib.hst_pair_stream_k_tiles(tiles, k_blocks, pairs, ctypes.byref(out)) == 0
+                assert out.value == pair_stream_k_tiles(tiles, k_blocks, pairs)
+    assert lib.hst_pair_stream_k_tiles(4, 4, 0, ctypes.byref(out)) == _native.HST_ERR_INVALID
