@@ -299,32 +299,11 @@ int split_plan(int64_t k, int bk, int requested, int* kb_per_split, int* splits)
   return HST_OK;
 }
 
-int stream_ctas_per_sm(int mp, int nt, int bk, int stages) {
-  const int smem = stages * (nt + mp) * bk * 2 + 2048;
-  const int by_smem = kSmemPerSm / (smem + kSmemReservedPerCta);
-  const int by_tmem = 512 / (mp <= 32 ? 32 : mp);
-  int c = by_smem < by_tmem ? by_smem : by_tmem;
-  if (c > 4) c = 4;
-  return c < 1 ? 1 : c;
-}
-
 // Clusters of `size` CTAs (one CTA per SM) a B200 keeps resident at once: its GPCs fit 74 pairs,
 // 33 clusters of four and 15 of eight (cudaOccupancyMaxActiveClusters), scaled to `sms`.
 int64_t resident_clusters(int size, int sms) {
   const int64_t per148 = size <= 1 ? 148 : size == 2 ? 74 : size <= 4 ? 33 : 15;
   return per148 * sms / 148;
-}
-
-int stream_cluster_ctas_per_sm(int mp, int nt, int bk, int stages) {
-  const int ring = stages * (nt + mp) * bk * 2;
-  const int partial = nt * mp * 4;
-  const int smem = (ring > partial ? ring : partial) + 2048;
-  const int by_smem = kSmemPerSm / (smem + kSmemReservedPerCta);
-  const int cols = (nt / 128) * mp;
-  const int by_tmem = 512 / (cols <= 32 ? 32 : cols);
-  int c = by_smem < by_tmem ? by_smem : by_tmem;
-  if (c > 4) c = 4;
-  return c < 1 ? 1 : c;
 }
 
 int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t m, int64_t n,
