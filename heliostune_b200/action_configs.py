@@ -158,10 +158,12 @@ class PairConfig:
             exact_int(getattr(self, name), context=f"pair config {name}", minimum=1)
         if self.block_m != 256:
             raise SchemaError("block_m must be 256 (two SMs x 128 rows)")
-        if self.block_n not in (128, 256):
-            raise SchemaError("block_n must be 128 or 256")
+        if self.block_n not in (128, 256, 512):
+            raise SchemaError("block_n must be 128, 256 or 512")
         if self.block_k not in (64, 128):
             raise SchemaError("block_k must be 64 or 128")
+        if self.block_n == 512 and (self.block_k != 64 or self.split_k > 1):
+            raise SchemaError("the 512-wide pair tile has block_k 64 and no cluster split-K")
         if self.num_warps not in (1, 2, 4, 8):
             raise SchemaError("num_warps must be one of 1, 2, 4, or 8")
         exact_int(self.split_k, context="pair config split_k", minimum=PAIR_STREAM_K)
@@ -309,18 +311,32 @@ def pair_stream_k_tiles(tiles: int, k_blocks: int, pairs: int) -> int:
     return shared if shared * k_blocks >= 2 * pairs else 0
 
 
+#: 512-wide pair tiles (a quarter fewer L2-to-SM bytes per FLOP, single-buffered accumulator),
+#: offered once the 256 x 512 tiles fill a wave of pairs; the stream-K form where they leave the
+#: last wave part-filled.
+PAIR_WIDE = ActionCandidate(PairConfig(256, 512, 64, 4, 4, 16))
+PAIR_WIDE_STREAM_K = ActionCandidate(PairConfig(256, 512, 64, 4, 4, 8, PAIR_STREAM_K))
+
+
 def pair_candidates_for(workload: Workload, sm_count: int = 148) -> tuple[ActionCandidate, ...]:
     """B200 CTA-pair candidates for ``M > 128`` (empty below)."""
     if workload.m < PAIR_M_MINIMUM:
         return ()
     tiles = -(-workload.m // 256) * -(-workload.n // 256)
+    wide_tiles = -(-workload.m // 256) * -(-workload.n // 512)
+    k_blocks = -(-workload.k // 64)
+    pairs = resident_clusters(2, sm_count)
     extra = ()
     if tiles <= 33:
         extra += (PAIR_SPLIT2,)
     if tiles <= 15:
         extra += (PAIR_SPLIT4,)
-    if pair_stream_k_tiles(tiles, -(-workload.k // 64), resident_clusters(2, sm_count)) > 0:
+    if pair_stream_k_tiles(tiles, k_blocks, pairs) > 0:
         extra += (PAIR_STREAM_K_CANDIDATE,)
+    if wide_tiles >= pairs:
+        extra += (PAIR_WIDE,)
+        if pair_stream_k_tiles(wide_tiles, k_blocks, pairs) > 0:
+            extra += (PAIR_WIDE_STREAM_K,)
     return _sorted((*PAIR_CANDIDATES, *extra))
 
 

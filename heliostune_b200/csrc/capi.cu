@@ -342,8 +342,12 @@ int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t 
     case HST_FAMILY_PAIR: {
       if (cfg->group_m < 1) return fail(HST_ERR_INVALID, "group_m must be positive");
       if (bm != 256) return fail(HST_ERR_UNSUPPORTED, "pair tiles have block_m 256");
-      if (bn != 128 && bn != 256) return fail(HST_ERR_UNSUPPORTED, "pair block_n must be 128 or 256");
+      if (bn != 128 && bn != 256 && bn != 512)
+        return fail(HST_ERR_UNSUPPORTED, "pair block_n must be 128, 256 or 512");
       if (bk != 64 && bk != 128) return fail(HST_ERR_UNSUPPORTED, "pair block_k must be 64 or 128");
+      if (bn == 512 && bk != 64) return fail(HST_ERR_UNSUPPORTED, "the 512-wide pair tile has block_k 64");
+      if (bn == 512 && cfg->split_k > 1)
+        return fail(HST_ERR_UNSUPPORTED, "the 512-wide pair tile has no cluster split-K (use stream-K)");
       if (cfg->split_k < HST_PAIR_STREAM_K || cfg->split_k > 4 || cfg->split_k == 3)
         return fail(HST_ERR_INVALID, "pair split_k must be -1 (stream-K), 0 (automatic), 1, 2 or 4");
       p->um = 128;
@@ -363,7 +367,7 @@ int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t 
         if (p->sk_tiles > 0) p->sk_pairs = static_cast<int>(max_pairs);
         break;
       }
-      int splits = cfg->split_k;
+      int splits = bn == 512 ? 1 : cfg->split_k;
       if (splits == 0) {
         // Split K while the tiles leave most SMs idle and a wave of (2, S) clusters holds them:
         // a B200 keeps at most 33 clusters of four and 15 of eight CTAs resident.
@@ -627,6 +631,8 @@ int dispatch_pair(const DeviceState& dev, const Plan& p, const Operands& o, uint
   HST_PAIR_CASE(256, 128)
   HST_PAIR_CASE(128, 128)
 #undef HST_PAIR_CASE
+  if (p.bn == 512 && p.bk == 64)
+    return launch_pair<512, 64, false>(dev, o, p.stages, p.group_m, 1, 0, stream, nullptr, &sk, p.sk_pairs);
   return fail(HST_ERR_UNSUPPORTED, "no pair kernel for N %d, K %d", p.bn, p.bk);
 }
 

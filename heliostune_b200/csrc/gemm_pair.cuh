@@ -43,11 +43,19 @@
 
 namespace hst {
 
+// BN = 512 ("wide"): two N = 256 UMMAs per K step into the two halves of TMEM, which then holds
+// one 128 x 512 FP32 accumulator per CTA instead of two 128 x 256 ones. Each SM moves 48 KB per
+// 64-deep K block for 2 x 128 x 256 x 64 multiply-adds -- a quarter fewer L2-to-SM bytes per
+// FLOP than the 256-wide tile -- at the price of the double-buffered accumulator: the epilogue
+// frees the first half as soon as it has drained it, and the UMMA issuer runs the next tile's
+// first-half UMMAs on the stages it holds until the second half is free too.
 template <int BN, int BK>
 struct PairShape {
-  static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
+  static_assert(BN == 128 || BN == 256 || BN == 512, "pair tiles are 256 x 128, 256 or 512");
   static_assert(BK == 64 || BK == 128, "BK must be 64 or 128");
-  static constexpr int kHalfN = BN / 2;
+  static_assert(BN != 512 || BK == 64, "the 512-wide tile uses BK 64");
+  static constexpr bool kWide = BN == 512;
+  static constexpr int kHalfN = BN / 2;         // B columns each CTA loads per tile
   static constexpr int kAtomsK = BK / 64;
   static constexpr int kAtomsN = kHalfN / 64;
   static constexpr int kABoxBytes = 128 * 128;  // 128 rows x 64 k
@@ -55,13 +63,18 @@ struct PairShape {
   static constexpr int kABytes = kAtomsK * kABoxBytes;
   static constexpr int kBBytes = kAtomsN * kBBoxBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;  // per CTA
-  static constexpr int kAccCols = BN;
-  static constexpr int kTmemCols = 2 * BN;  // two accumulators
+  static constexpr int kUmmaN = kWide ? 256 : BN;          // N of one UMMA
+  static constexpr int kAccCols = kWide ? 0 : BN;          // column offset of accumulator 1
+  static constexpr int kTmemCols = BN == 128 ? 256 : 512;  // two accumulators, or one wide one
   static constexpr int kEpilogueBytes = 4 * 2 * kEpilogueStageBytes;
   static constexpr int kBarrierBytes = 256 + 16 * kMaxStages;
-  static constexpr uint32_t kIdesc = umma_idesc_f16(256, BN, false, true);
+  static constexpr uint32_t kIdesc = umma_idesc_f16(256, kUmmaN, false, true);
   static constexpr int smem_bytes(int stages) {
     return 1024 + stages * kStageBytes + kEpilogueBytes + kBarrierBytes;
+  }
+  // Tile column of this CTA's B atom `na`: the 256-wide UMMAs each take 128 columns per CTA.
+  __host__ __device__ static constexpr int b_col(int rank, int na) {
+    return kWide ? (na / 2) * 256 + rank * 128 + (na % 2) * 64 : rank * kHalfN + na * 64;
   }
 };
 
@@ -223,7 +236,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       int pm, pn;
       grouped_tile(tile, args.tiles_m, args.tiles_n, args.group_m, pm, pn);
       const int m0 = pm * 256 + static_cast<int>(rank) * 128;
-      const int n0 = pn * BN + static_cast<int>(rank) * S::kHalfN;
+      const int n0 = pn * BN;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
           raise_abort(args.status, abort_flag, kStatusProducerTimeout);
@@ -245,7 +258,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
 #pragma unroll
         for (int na = 0; na < S::kAtomsN; ++na) {
           tma_load_2d_pair(st + S::kABytes + na * S::kBBoxBytes, &map_b, leader_full,
-                           n0 + 64 * na, k0, policy);
+                           n0 + S::b_col(static_cast<int>(rank), na), k0, policy);
         }
         if (++stage == stages) {
           stage = 0;
@@ -270,6 +283,24 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     bool ok = true;
     PairWork work(args, sk_tiles, pair, pairs);
     int tile, kb0, kb1;
+    // UMMAs of one K block of stage `st` into accumulator columns [col, col + kUmmaN); B atoms
+    // from `b_atom` on. `first`: the segment's first K block (overwrite instead of accumulate).
+    auto issue = [&](int st, uint32_t col, int b_atom, bool first) {
+      const uint32_t a_base = smem_addr(ring + st * S::kStageBytes);
+      const uint32_t b_base = a_base + S::kABytes + b_atom * S::kBBoxBytes;
+#pragma unroll
+      for (int kk = 0; kk < BK / 16; ++kk) {
+        const uint64_t adesc =
+            smem_desc(a_base + (kk >> 2) * S::kABoxBytes + (kk & 3) * 32, 16, 1024);
+        const uint64_t bdesc = smem_desc(b_base + kk * 2048, S::kBBoxBytes, 1024);
+        umma_f16_pair(tmem_base + col, adesc, bdesc, S::kIdesc, (!first || kk != 0) ? 1u : 0u);
+      }
+    };
+    auto release_stage = [&](int st) {
+      const uint32_t own_empty = smem_addr(&empty[st]);
+      umma_commit_pair(own_empty);
+      umma_commit_pair(map_to_rank(own_empty, crank | 1u));
+    };
     while (ok && next_segment(work, tile, kb0, kb1)) {
       if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort_flag)) {
         raise_abort(args.status, abort_flag, kStatusMmaTimeout);
@@ -277,7 +308,10 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         break;
       }
       tc_fence_after_sync();
-      const uint32_t d_base = tmem_base + acc * S::kAccCols;
+      // Wide tile: the second accumulator half may still be draining. Its UMMAs wait, on the
+      // stages this thread holds, until the epilogue frees it or every stage is held.
+      bool second = !S::kWide;
+      int held = 0, held_stage = stage;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&full[stage], phase, abort_flag)) {
           raise_abort(args.status, abort_flag, kStatusMmaTimeout);
@@ -285,28 +319,58 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           break;
         }
         tc_fence_after_sync();
-        const uint32_t a_base = smem_addr(ring + stage * S::kStageBytes);
-        const uint32_t b_base = a_base + S::kABytes;
-#pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint64_t adesc =
-              smem_desc(a_base + (kk >> 2) * S::kABoxBytes + (kk & 3) * 32, 16, 1024);
-          const uint64_t bdesc = smem_desc(b_base + kk * 2048, S::kBBoxBytes, 1024);
-          umma_f16_pair(d_base, adesc, bdesc, S::kIdesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+        issue(stage, static_cast<uint32_t>(acc * S::kAccCols), 0, kb == kb0);
+        if constexpr (S::kWide) {
+          if (second) {
+            issue(stage, 256u, 2, kb == kb0);
+            release_stage(stage);
+          } else {
+            ++held;
+            if (held == stages || mbar_test_wait(&tmem_empty[1], acc_phase ^ 1u)) {
+              if (!mbar_wait(&tmem_empty[1], acc_phase ^ 1u, abort_flag)) {
+                raise_abort(args.status, abort_flag, kStatusMmaTimeout);
+                ok = false;
+                break;
+              }
+              tc_fence_after_sync();
+              second = true;
+              for (int j = 0; j < held; ++j) {
+                const int st = (held_stage + j) % stages;
+                issue(st, 256u, 2, j == 0);
+                release_stage(st);
+              }
+              held = 0;
+            }
+          }
+        } else {
+          release_stage(stage);
         }
-        const uint32_t own_empty = smem_addr(&empty[stage]);
-        umma_commit_pair(own_empty);
-        umma_commit_pair(map_to_rank(own_empty, crank | 1u));
         if (++stage == stages) {
           stage = 0;
           phase ^= 1u;
+        }
+      }
+      if (ok && !second) {
+        // A segment shorter than the ring: the held K blocks' second halves.
+        if (!mbar_wait(&tmem_empty[1], acc_phase ^ 1u, abort_flag)) {
+          raise_abort(args.status, abort_flag, kStatusMmaTimeout);
+          ok = false;
+        } else {
+          tc_fence_after_sync();
+          for (int j = 0; j < held; ++j) {
+            const int st = (held_stage + j) % stages;
+            issue(st, 256u, 2, j == 0);
+            release_stage(st);
+          }
         }
       }
       if (!ok) break;
       const uint32_t own_full = smem_addr(&tmem_full[acc]);
       umma_commit_pair(own_full);
       umma_commit_pair(map_to_rank(own_full, crank | 1u));
-      if (++acc == 2) {
+      if (S::kWide) {
+        acc_phase ^= 1u;
+      } else if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
       }
@@ -331,6 +395,19 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       return sk.partials + (static_cast<size_t>(q) * 2 + rank) * (kChunks * 128 * 4);
     };
     auto flag_of_pair = [&](int q) { return sk.flags + (static_cast<size_t>(q) * 2 + rank) * 4 + quarter; };
+    // Reports accumulator `which` (or, for the wide tile, accumulator half `which`) drained, on
+    // the leader's barrier.
+    auto release_acc = [&](int which) {
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0) {
+          mbar_arrive(&tmem_empty[which]);
+        } else {
+          mbar_arrive_cluster(map_to_rank(smem_addr(&tmem_empty[which]), leader));
+        }
+      }
+    };
     PairWork work(args, sk_tiles, pair, pairs);
     int tile, kb0, kb1;
     while (next_segment(work, tile, kb0, kb1)) {
@@ -346,6 +423,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       tc_fence_after_sync();
       const uint32_t lane_tmem = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * S::kAccCols;
       const int64_t tile_end = int64_t(tile + 1) * args.k_blocks;  // stream-K iteration after the tile
+      bool released0 = !S::kWide;  // wide tile: first accumulator half reported drained
       if (kb0 > 0) {
         // ---- a later K range of a shared tile: publish it as an FP32 partial ----
         float* slot = slot_of_pair(pair);
@@ -358,6 +436,10 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           for (int j = 0; j < 8; ++j) {
             st_global_v4(slot + (static_cast<size_t>(c / 4 + j) * 128 + row) * 4, v[4 * j], v[4 * j + 1],
                          v[4 * j + 2], v[4 * j + 3]);
+          }
+          if (!released0 && c + 32 == 256) {
+            release_acc(0);
+            released0 = true;
           }
         }
         __threadfence();
@@ -385,6 +467,10 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           tmem_ld_32x32b_x32(taddr, lo);
           tmem_ld_32x32b_x32(taddr + 32, hi);
           tmem_ld_wait();
+          if (!released0 && c * 64 + 64 == 256) {
+            release_acc(0);
+            released0 = true;
+          }
           if (finisher) {
             // Add the later K ranges in K order (pair - 1 first).
             int64_t pos = work.it;
@@ -449,18 +535,16 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           buf ^= 1;
         }
       }
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) {
-        if (rank == 0) {
-          mbar_arrive(&tmem_empty[acc]);
-        } else {
-          mbar_arrive_cluster(map_to_rank(smem_addr(&tmem_empty[acc]), leader));
-        }
-      }
-      if (++acc == 2) {
-        acc = 0;
+      if (!released0) release_acc(0);
+      if (S::kWide) {
+        release_acc(1);
         acc_phase ^= 1u;
+      } else {
+        release_acc(acc);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
       }
     }
     if (lane == 0) bulk_wait_group<0>();

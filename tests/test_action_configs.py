@@ -19,6 +19,7 @@ from heliostune_b200.action_configs import (
     action_set_manifest,
     b200_candidates_for,
     candidates_for,
+    PairConfig,
     pair_candidates_for,
     pair_stream_k_tiles,
     split_plan,
@@ -247,4 +248,19 @@ def test_pair_stream_k_rule() -> None:
     assert pair_stream_k_tiles(3, 5, 74) == 0  # under two K blocks per pair
     w = Workload(2048, 4096, 4096, "x", "y", "z")
     assert any(c.key.endswith("-streamk") for c in pair_candidates_for(w))
-    assert not any(c.key.endswith("-streamk") for c in pair_candidates_for(replace(w, m=8192, n=9472)))
+    # 32 x 37 tiles of 256 x 256 are 16 whole waves
+    assert "pair:pair-m256n256k64-w4s6g8-streamk" not in {c.key for c in pair_candidates_for(replace(w, m=8192, n=9472))}
+
+
+def test_wide_pair_candidates_need_a_full_wave() -> None:
+    def keys(m: int, n: int, k: int) -> set[str]:
+        return {c.key for c in pair_candidates_for(Workload(m, n, k, "x", "y", "z"))}
+
+    assert "pair:pair-m256n512k64-w4s4g16" not in keys(512, 4096, 4096)  # 16 wide tiles
+    assert "pair:pair-m256n512k64-w4s4g16" in keys(8192, 4096, 4096)  # 256 wide tiles
+    assert "pair:pair-m256n512k64-w4s4g8-streamk" in keys(8192, 4096, 14336)  # 256 = 3 x 74 + 34
+    assert "pair:pair-m256n512k64-w4s4g8-streamk" not in keys(8192, 37888, 3584)  # 32 x 74 exactly
+    with pytest.raises(SchemaError):
+        PairConfig(256, 512, 128, 4, 4, 8)
+    with pytest.raises(SchemaError):
+        PairConfig(256, 512, 64, 4, 4, 8, 2)

@@ -163,6 +163,34 @@ def test_pair_stream_k(block_n: int, shape: tuple[int, int, int]) -> None:
         assert torch.equal(first.view(torch.int16), launch(a, b, candidate).view(torch.int16))
 
 
+@pytest.mark.parametrize(
+    "config",
+    (PairConfig(256, 512, 64, 4, 4, 16), PairConfig(256, 512, 64, 4, 4, 8, PAIR_STREAM_K)),
+    ids=lambda c: ActionCandidate(c).key,
+)
+@pytest.mark.parametrize(
+    "shape",
+    (
+        (256, 512, 64),  # one tile, one K block
+        (300, 1000, 520),  # ragged: the second UMMA of the last column tile is half outside
+        (1000, 2056, 777),  # 8 columns past the last full tile
+        (2048, 3584, 3584),  # 56 tiles: under one wave of pairs
+        (512, 28672, 1024),  # 112 tiles: a wave and a half
+        (8192, 4096, 512),  # 256 tiles, shallow K: the accumulator halves turn over fast
+    ),
+    ids=lambda s: "x".join(map(str, s)),
+)
+def test_pair_wide_tile(config: PairConfig, shape: tuple[int, int, int]) -> None:
+    m, n, k = shape
+    g = torch.Generator(device="cuda").manual_seed(m * 3 + n)
+    a = scaled_normal((m, k), k, g)
+    b = scaled_normal((k, n), k, g)
+    candidate = ActionCandidate(config)
+    first = launch(a, b, candidate)
+    assert_gemm_parity(first, a, b)
+    assert torch.equal(first.view(torch.int16), launch(a, b, candidate).view(torch.int16))
+
+
 def test_pair_stream_k_ignores_stale_workspace_contents() -> None:
     lib = _native.library()
     m, n, k = 512, 4096, 2048
@@ -308,6 +336,7 @@ def test_full_size_grid_shapes(workload: Workload) -> None:
         ActionCandidate(StreamConfig(128, 256, 64, 4, 3, 4)),
         ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8)),
         ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8, PAIR_STREAM_K)),
+        ActionCandidate(PairConfig(256, 512, 64, 4, 4, 16)),
     ],
     ids=lambda c: c.key,
 )
