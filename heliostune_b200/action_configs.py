@@ -262,11 +262,17 @@ def stream_candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:
     if workload.m > STREAM_M_LIMIT:
         return ()
     bm = stream_block_m(workload.m)
+    wide = ()
+    if bm in (64, 128):
+        # 256 columns per CTA: both column atoms share each A^T tile, halving the A bytes per
+        # byte of B that matter once M approaches the column tile.
+        wide = (ActionCandidate(StreamConfig(bm, 256, 64, 4, 4, 0)),)
     return _sorted(
         (
             ActionCandidate(StreamConfig(bm, 128, 64, 4, 8, 0)),
             ActionCandidate(StreamConfig(bm, 128, 128, 4, 4, 0)),
             ActionCandidate(StreamConfig(bm, 128, 64, 4, 4, 0)),
+            *wide,
         )
     )
 
@@ -340,11 +346,27 @@ def pair_candidates_for(workload: Workload, sm_count: int = 148) -> tuple[Action
     return _sorted((*PAIR_CANDIDATES, *extra))
 
 
+#: Frozen candidates the B200 tuner keeps beside the B200 families. The others never won a grid
+#: shape on the B200 (the CTA-pair family beats every single-SM tile above M = 128, the stream
+#: family every tile and all but one split-K configuration below); leaving them out gives the
+#: bandit's eight probes to the variants that compete.
+B200_FROZEN_KEPT = frozenset(
+    {
+        "tile:m128n128k128-w8s3g8",
+        "tile:m128n256k64-w8s4g8",
+        "split_k:m16n64k64-w4s3-split4",
+        "split_k:m16n128k64-w4s3-split4",
+    }
+)
+
+
 def b200_candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:
-    """Everything the B200 tuner may probe: the frozen set plus the B200 families."""
-    return _sorted(
-        (*candidates_for(workload), *stream_candidates_for(workload), *pair_candidates_for(workload))
-    )
+    """Everything the B200 tuner may probe: the frozen candidates of :data:`B200_FROZEN_KEPT`
+    that apply to the workload, plus the B200 families."""
+    frozen = tuple(c for c in candidates_for(workload) if c.key in B200_FROZEN_KEPT)
+    if workload.m <= 31:
+        frozen = tuple(c for c in frozen if c.family == "split_k")
+    return _sorted((*frozen, *stream_candidates_for(workload), *pair_candidates_for(workload)))
 
 
 def action_set_manifest() -> dict[str, list[dict[str, Any]]]:

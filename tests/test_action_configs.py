@@ -11,6 +11,7 @@ import pytest
 
 from heliostune_b200.action_configs import (
     ALL_CANDIDATES,
+    B200_FROZEN_KEPT,
     NON_SPLIT_CANDIDATES,
     SPLIT_K_CANDIDATES,
     ActionCandidate,
@@ -162,7 +163,11 @@ def test_stream_family() -> None:
     w = GRID_WORKLOADS[0]
     assert all(c.family == "stream" for c in stream_candidates_for(w))
     assert stream_candidates_for(replace(w, m=512)) == ()
-    assert set(candidates_for(w)) <= set(b200_candidates_for(w))
+    # the B200 pool keeps the split-K candidates of the frozen set that ever won on a B200
+    kept = {c for c in candidates_for(w) if c.key in B200_FROZEN_KEPT and c.family == "split_k"}
+    assert kept and kept <= set(b200_candidates_for(w))
+    assert not any(c.family in ("tile", "persistent") for c in b200_candidates_for(w))  # M = 1
+    assert set(stream_candidates_for(w)) <= set(b200_candidates_for(w))
     with pytest.raises(SchemaError):
         StreamConfig(16, 64, 64, 4, 8, 0)
     with pytest.raises(SchemaError):
