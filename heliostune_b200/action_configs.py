@@ -81,9 +81,9 @@ class StreamConfig:
     A CTA owns ``block_n`` columns of C (128, or 256 as two UMMA atoms sharing the A tile, for
     ``block_m`` 64 or 128) and all M rows, padded to ``block_m`` (a power of two >= 16, the UMMA
     N of the swapped MMA). ``block_k`` and ``num_stages`` shape the TMA ring. ``split_k`` CTAs
-    (1, 2, 4 or 8; 0 asks for the largest that keeps one wave of CTAs on the SMs) divide K and form
-    a thread-block cluster that sums their FP32 partials in split order through distributed
-    shared memory, so no workspace and no second kernel are needed.
+    (1..8; 0 asks for the count that puts the most CTAs in one wave, see :func:`stream_splits`)
+    divide K and form a thread-block cluster that sums their FP32 partials in split order through
+    distributed shared memory, so no workspace and no second kernel are needed.
     """
 
     block_m: int
@@ -108,8 +108,8 @@ class StreamConfig:
             raise SchemaError("block_n 256 needs block_m 64 or 128")
         if self.block_k not in (64, 128):
             raise SchemaError("block_k must be 64 or 128")
-        if self.split_k not in (0, 1, 2, 4, 8):
-            raise SchemaError("split_k must be 0 (automatic), 1, 2, 4 or 8")
+        if self.split_k > 8:
+            raise SchemaError("split_k must be 0 (automatic) or 1..8")
         if self.num_warps not in (1, 2, 4, 8):
             raise SchemaError("num_warps must be one of 1, 2, 4, or 8")
 
@@ -423,27 +423,32 @@ def split_plan(k: int, block_k: int, splits: int) -> tuple[int, int]:
 def resident_clusters(size: int, sm_count: int) -> int:
     """Clusters of ``size`` CTAs (one per SM) a B200 keeps resident at once.
 
-    ``cudaOccupancyMaxActiveClusters`` on the 148-SM B200 gives 148, 74, 33 and 15 for clusters
-    of 1, 2, 4 and 8 CTAs (the GPCs fit fewer large clusters); scaled to ``sm_count``.
+    ``cudaOccupancyMaxActiveClusters`` on the 148-SM B200 gives 148, 74, 45, 33, 26, 22, 15 and
+    15 for clusters of 1 to 8 CTAs (the GPCs fit fewer large clusters); scaled to ``sm_count``.
     """
-    per148 = {1: 148, 2: 74, 4: 33, 8: 15}[size]
+    per148 = {1: 148, 2: 74, 3: 45, 4: 33, 5: 26, 6: 22, 7: 15, 8: 15}[size]
     return per148 * sm_count // 148
 
 
 def stream_splits(m: int, n: int, k: int, config: StreamConfig, sm_count: int) -> int:
     """The cluster size (K splits) a :class:`StreamConfig` launches with on ``sm_count`` SMs.
 
-    Automatic: the largest power of two <= 8 whose clusters are all resident in one wave. Then,
-    as the launcher does, halve until every split owns K blocks and all but the last the same
-    number.
+    Automatic: of 1..8, the split count giving the most CTAs (column tiles x splits) whose
+    clusters are all resident in one wave, the smallest on a tie. As the launcher does, a count
+    must give every split K blocks and all but the last the same number (else the next lower).
     """
     k_blocks = -(-k // config.block_k)
+
+    def k_splits_ok(s: int) -> bool:
+        return s <= k_blocks and -(-k_blocks // -(-k_blocks // s)) == s
+
     splits = config.split_k
     if splits == 0:
         n_tiles = -(-n // config.block_n)
-        splits = 8
-        while splits > 1 and n_tiles > resident_clusters(splits, sm_count):
-            splits //= 2
-    while splits > 1 and (splits > k_blocks or -(-k_blocks // -(-k_blocks // splits)) != splits):
-        splits //= 2
+        splits = 1
+        for s in range(2, 9):
+            if n_tiles <= resident_clusters(s, sm_count) and k_splits_ok(s) and s > splits:
+                splits = s
+    while splits > 1 and not k_splits_ok(splits):
+        splits -= 1
     return splits

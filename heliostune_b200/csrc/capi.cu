@@ -299,11 +299,12 @@ int split_plan(int64_t k, int bk, int requested, int* kb_per_split, int* splits)
   return HST_OK;
 }
 
-// Clusters of `size` CTAs (one CTA per SM) a B200 keeps resident at once: its GPCs fit 74 pairs,
-// 33 clusters of four and 15 of eight (cudaOccupancyMaxActiveClusters), scaled to `sms`.
+// Clusters of `size` CTAs (one CTA per SM) a B200 keeps resident at once, as
+// cudaOccupancyMaxActiveClusters reports them for 1..8 CTAs (its GPCs fit 74 pairs but only 33
+// clusters of four and 15 of seven or eight), scaled to `sms`.
 int64_t resident_clusters(int size, int sms) {
-  const int64_t per148 = size <= 1 ? 148 : size == 2 ? 74 : size <= 4 ? 33 : 15;
-  return per148 * sms / 148;
+  static constexpr int64_t kPer148[9] = {148, 148, 74, 45, 33, 26, 22, 15, 15};
+  return kPer148[size < 1 ? 1 : (size > 8 ? 8 : size)] * sms / 148;
 }
 
 int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t m, int64_t n,
@@ -407,23 +408,27 @@ int make_plan(const hst_gemm_config* cfg, const View& a, const View& b, int64_t 
       if (bn == 256 && (bm < 64 || bm > 128))
         return fail(HST_ERR_UNSUPPORTED, "stream block_n 256 needs block_m 64 or 128");
       if (bk != 64 && bk != 128) return fail(HST_ERR_UNSUPPORTED, "stream block_k must be 64 or 128");
-      if (cfg->split_k < 0 || cfg->split_k > 8 || (cfg->split_k & (cfg->split_k - 1)))
-        return fail(HST_ERR_INVALID, "stream split_k must be 0 (automatic), 1, 2, 4 or 8");
+      if (cfg->split_k < 0 || cfg->split_k > 8)
+        return fail(HST_ERR_INVALID, "stream split_k must be 0 (automatic) or 1..8");
       p->nt = bn;
       p->mp = bm;
       p->bk = bk;
       p->stages = cfg->num_stages < 2 ? 2 : (cfg->num_stages > kStreamMaxStages ? kStreamMaxStages : cfg->num_stages);
       const int64_t k_blocks = cdiv(k, bk);
       int splits = cfg->split_k;
-      if (splits == 0) {
-        // Largest power of two <= 8 whose clusters are all resident in one wave.
-        const int64_t n_tiles = cdiv(n, bn);
-        splits = 8;
-        while (splits > 1 && n_tiles > resident_clusters(splits, sms)) splits /= 2;
-      }
       // Every split must own at least one K block and all splits the same count but the last.
-      while (splits > 1 && (splits > k_blocks || cdiv(k_blocks, cdiv(k_blocks, splits)) != splits))
-        splits /= 2;
+      auto k_splits_ok = [&](int s) { return s <= k_blocks && cdiv(k_blocks, cdiv(k_blocks, s)) == s; };
+      if (splits == 0) {
+        // The most CTAs in one wave: the S (1..8) with the largest tiles x S whose clusters are
+        // all resident at once, the smallest such S on a tie.
+        const int64_t n_tiles = cdiv(n, bn);
+        splits = 1;
+        for (int s = 2; s <= 8; ++s) {
+          if (n_tiles <= resident_clusters(s, sms) && k_splits_ok(s) && s * n_tiles > splits * n_tiles)
+            splits = s;
+        }
+      }
+      while (splits > 1 && !k_splits_ok(splits)) --splits;
       p->splits = splits;
       p->kb_per_split = static_cast<int>(cdiv(k_blocks, splits));
       break;
@@ -716,8 +721,8 @@ int launch_stream_cluster(const DeviceState& dev, const Operands& o, int stages,
   using S = ClusterStreamShape<NA, MP, BK>;
   static std::atomic<uint64_t> smem_done{0};
   HST_TRY(allow_smem(stream_cluster_kernel<NA, MP, BK>, smem_done));
-  while (stages > 2 && S::smem_bytes(stages) > kMaxDynamicSmem) --stages;
-  if (S::smem_bytes(stages) > kMaxDynamicSmem)
+  while (stages > 2 && S::smem_bytes(stages, splits) > kMaxDynamicSmem) --stages;
+  if (S::smem_bytes(stages, splits) > kMaxDynamicSmem)
     return fail(HST_ERR_UNSUPPORTED, "stream tile does not fit shared memory");
   CUtensorMap ma_, mb_;
   HST_TRY(encode_tiled_2d(&ma_, o.a, o.k, o.m, o.lda, 64, MP));
@@ -736,7 +741,7 @@ int launch_stream_cluster(const DeviceState& dev, const Operands& o, int stages,
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(static_cast<unsigned>(cdiv(o.n, S::kNT)), static_cast<unsigned>(splits));
   lc.blockDim = dim3(kStreamThreads);
-  lc.dynamicSmemBytes = smem_for_tmem(S::smem_bytes(stages), S::kTmemCols);
+  lc.dynamicSmemBytes = smem_for_tmem(S::smem_bytes(stages, splits), S::kTmemCols);
   lc.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;

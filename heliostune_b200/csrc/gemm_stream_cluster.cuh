@@ -4,13 +4,14 @@
 // UMMA N = MP rows of A), with two changes for small M:
 //   * a CTA may own NA = 2 column atoms (256 columns of C): both UMMAs share the A^T tile of a
 //     stage, halving the A bytes each CTA pulls per byte of B;
-//   * the S CTAs that split one column tile's K range form a thread-block cluster (1, S, 1);
-//     CTA r owns columns [r*NT/S, (r+1)*NT/S) of the tile. Once every CTA's main loop is done
-//     (cluster barrier: all rings drained), each CTA pushes every column slice of its FP32
-//     accumulator from TMEM into the owner's shared memory (remote stores, slot = source split);
-//     after a second barrier each owner sums its S slots in split order 0..S-1 from local shared
-//     memory and writes FP16 C. No workspace, no second kernel, no atomics; the result is
-//     bitwise reproducible.
+//   * the S CTAs (1 <= S <= 8) that split one column tile's K range form a thread-block cluster
+//     (1, S, 1); CTA r owns columns [r*W, min((r+1)*W, NT)) of the tile, W = ceil(NT/S) rounded
+//     up to a multiple of 4. Once every CTA's main loop is done (cluster barrier: all rings
+//     drained), each CTA pushes every column slice of its FP32 accumulator from TMEM into the
+//     owner's shared memory (remote stores, slot = source split, row-major [MP][W] so that a
+//     warp's store covers 128 contiguous bytes); after a second barrier each owner sums its S
+//     slots in split order 0..S-1 from local shared memory and writes FP16 C. No workspace, no
+//     second kernel, no atomics; the result is bitwise reproducible.
 // With S = 1 the epilogue writes C straight from TMEM.
 #pragma once
 
@@ -42,14 +43,23 @@ struct ClusterStreamShape {
   static constexpr int kWBytes = kAtomsN * kWBoxBytes;
   static constexpr int kXBytes = kAtomsK * kXBoxBytes;
   static constexpr int kStageBytes = kWBytes + kXBytes;
-  static constexpr int kPartialBytes = kNT * MP * 4;
+  // Columns each CTA of an S-CTA cluster owns (the last may own fewer).
+  __host__ __device__ static constexpr int owner_cols(int splits) {
+    return ((kNT + splits - 1) / splits + 3) / 4 * 4;
+  }
+  // The S exchange slots, [MP][owner_cols] FP32 each.
+  __host__ __device__ static constexpr int exchange_bytes(int splits) {
+    return splits * owner_cols(splits) * MP * 4;
+  }
   static constexpr int kCols = NA * MP;
   static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128 : kCols <= 256 ? 256 : 512;
   static constexpr uint32_t kIdesc = umma_idesc_f16(128, MP, true, false);
   static constexpr int kBarrierBytes = 256 + 16 * kStreamMaxStages;
-  static constexpr int smem_bytes(int stages) {
-    const int ring = stages * kStageBytes;
-    return 1024 + (ring > kPartialBytes ? ring : kPartialBytes) + kBarrierBytes;
+  __host__ __device__ static constexpr int ring_bytes(int stages, int splits) {
+    return stages * kStageBytes > exchange_bytes(splits) ? stages * kStageBytes : exchange_bytes(splits);
+  }
+  static constexpr int smem_bytes(int stages, int splits) {
+    return 1024 + ring_bytes(stages, splits) + kBarrierBytes;
   }
 };
 
@@ -63,9 +73,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int stages = args.stages;
   uint8_t* ring = smem;  // after the main loop it holds this CTA's FP32 partial [MP][NT]
-  const int ring_bytes = stages * S::kStageBytes > S::kPartialBytes ? stages * S::kStageBytes
-                                                                     : S::kPartialBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + ring_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + S::ring_bytes(stages, args.splits));
   uint64_t* full = bars;
   uint64_t* empty = bars + kStreamMaxStages;
   uint64_t* tmem_full = bars + 2 * kStreamMaxStages;
@@ -187,8 +195,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 
   constexpr int kChunk = MP >= 32 ? 32 : 16;
   const int splits = args.splits;
-  const int cols = S::kNT / splits;           // columns of C each CTA of the cluster owns
-  const int slot_bytes = MP * cols * 4;       // one source split's slice, FP32 [MP][cols]
+  const int cols = S::owner_cols(splits);            // columns of C each CTA of the cluster owns
+  const int slot_bytes = MP * cols * 4;              // one source split's slice, FP32 [MP][cols]
   const uint32_t base = smem_addr(partial);
   if (splits > 1) cluster_sync();  // every main loop is done: all rings can receive
   if (warp >= 2 && have_result) {
@@ -239,7 +247,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     cluster_sync();  // every slice has arrived
     // ---- reduce locally in split order and write FP16 C ----
     const int rank = static_cast<int>(cluster_ctarank());
-    const int quads = cols / 4;
+    const int own_cols = min(cols, S::kNT - rank * cols);  // the last owner may have fewer
+    const int quads = own_cols / 4;
     const int items = args.m * quads;
     const bool vec_store = (args.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(args.c) & 7) == 0);
     for (int i = threadIdx.x; i < items; i += blockDim.x) {

@@ -173,7 +173,7 @@ def test_stream_family() -> None:
     with pytest.raises(SchemaError):
         StreamConfig(16, 256, 64, 4, 8, 0)
     with pytest.raises(SchemaError):
-        StreamConfig(16, 128, 64, 4, 8, 3)
+        StreamConfig(16, 128, 64, 4, 8, 9)
     # The automatic split is the largest power of two <= 8 whose clusters are all resident
     # (148 / 74 / 33 / 15 clusters of 1 / 2 / 4 / 8 CTAs on a B200).
     config = StreamConfig(16, 128, 64, 4, 8, 0)
@@ -181,6 +181,9 @@ def test_stream_family() -> None:
     assert stream_splits(1, 1024, 18944, config, 148) == 8  # 8 tiles: 8 clusters of eight
     assert stream_splits(1, 37888, 3584, config, 148) == 1  # 296 tiles already fill the GPU
     assert stream_splits(1, 8192, 4096, config, 148) == 2  # 64 tiles: 64 pairs
+    assert stream_splits(1, 4608, 4096, config, 148) == 3  # 36 tiles: 36 of the 45 clusters of three
+    assert stream_splits(64, 4096, 4096, StreamConfig(64, 256, 64, 4, 4, 0), 148) == 6  # 16 tiles
+    assert stream_splits(64, 6144, 4096, StreamConfig(64, 256, 64, 4, 4, 0), 148) == 5  # 24 tiles
     # every split owns K blocks: K = 100 is two blocks of 64
     assert stream_splits(1, 256, 100, StreamConfig(16, 128, 64, 4, 8, 8), 148) == 2
 

@@ -102,9 +102,25 @@ def test_stream_family(m: int) -> None:
     assert candidates
     for candidate in candidates:
         assert_gemm_parity(launch(a, b, candidate), a, b)
-    for split in (1, 2, 4, 8):
+    for split in (1, 2, 3, 4, 5, 6, 7, 8):
         fixed = ActionCandidate(StreamConfig(stream_block_m(m), 128, 64, 4, 4, split))
         assert_gemm_parity(launch(a, b, fixed), a, b)
+
+
+@pytest.mark.parametrize("split", (3, 5, 6, 7))
+@pytest.mark.parametrize("block_n", (128, 256))
+@pytest.mark.parametrize("shape", ((64, 4608, 3584), (100, 1000, 1000), (128, 6144, 4096)), ids=lambda s: "x".join(map(str, s)))
+def test_stream_odd_cluster_sizes(split: int, block_n: int, shape: tuple[int, int, int]) -> None:
+    """Clusters of 3, 5, 6 and 7 CTAs: the last owner holds fewer columns than the others."""
+    m, n, k = shape
+    g = torch.Generator(device="cuda").manual_seed(m + split)
+    a = scaled_normal((m, k), k, g)
+    b = scaled_normal((k, n), k, g)
+    bm = stream_block_m(m) if block_n == 128 else (64 if m <= 64 else 128)
+    candidate = ActionCandidate(StreamConfig(bm, block_n, 64, 4, 4, split))
+    first = launch(a, b, candidate)
+    assert_gemm_parity(first, a, b)
+    assert torch.equal(first.view(torch.int16), launch(a, b, candidate).view(torch.int16))
 
 
 @pytest.mark.parametrize("candidate", PAIR_CANDIDATES, ids=lambda c: c.key)
