@@ -6,12 +6,18 @@
 //     stage, halving the A bytes each CTA pulls per byte of B;
 //   * the S CTAs (1 <= S <= 8) that split one column tile's K range form a thread-block cluster
 //     (1, S, 1); CTA r owns columns [r*W, min((r+1)*W, NT)) of the tile, W = ceil(NT/S) rounded
-//     up to a multiple of 4. Once every CTA's main loop is done (cluster barrier: all rings
-//     drained), each CTA pushes every column slice of its FP32 accumulator from TMEM into the
-//     owner's shared memory (remote stores, slot = source split, row-major [MP][W] so that a
-//     warp's store covers 128 contiguous bytes); after a second barrier each owner sums its S
-//     slots in split order 0..S-1 from local shared memory and writes FP16 C. No workspace, no
-//     second kernel, no atomics; the result is bitwise reproducible.
+//     up to a multiple of 4. Each CTA pushes every column slice of its FP32 accumulator from TMEM
+//     into the owner's shared memory (remote stores, slot = source split, row-major [MP][W] so
+//     that a warp's store covers 128 contiguous bytes); each owner sums its S slots in split
+//     order 0..S-1 and writes FP16 C. Two ways to meet, by accumulator height:
+//       - MP <= 64 (a few stores per thread): asynchronous stores whose bytes complete on the
+//         owner's receive mbarrier, pushed as soon as the CTA's own accumulator is complete
+//         when the slots fit beside the TMA ring ("early"; a cluster barrier armed at launch
+//         guarantees every receive barrier exists), else into the drained ring after a
+//         cluster barrier;
+//       - MP >= 128: plain remote stores into the drained ring between two cluster barriers
+//         (cheaper per byte than the asynchronous stores once each thread sends 128 words).
+//     No workspace, no second kernel, no atomics; the result is bitwise reproducible.
 // With S = 1 the epilogue writes C straight from TMEM.
 #pragma once
 
@@ -25,6 +31,7 @@ struct ClusterStreamArgs {
   int kb_per_split;
   int splits;  // cluster size along y
   int stages;
+  int early;   // exchange slots beside the ring (1) or in it after the main loops (0)
   int* status;
   __half* c;
   int64_t ldc;
@@ -55,11 +62,14 @@ struct ClusterStreamShape {
   static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128 : kCols <= 256 ? 256 : 512;
   static constexpr uint32_t kIdesc = umma_idesc_f16(128, MP, true, false);
   static constexpr int kBarrierBytes = 256 + 16 * kStreamMaxStages;
-  __host__ __device__ static constexpr int ring_bytes(int stages, int splits) {
-    return stages * kStageBytes > exchange_bytes(splits) ? stages * kStageBytes : exchange_bytes(splits);
+  static constexpr bool kAsyncPush = MP <= 64;  // see the file comment
+  // Shared memory below the barriers: ring and exchange side by side, or overlaid.
+  __host__ __device__ static constexpr int data_bytes(int stages, int splits, bool early) {
+    return early ? stages * kStageBytes + exchange_bytes(splits)
+                 : (stages * kStageBytes > exchange_bytes(splits) ? stages * kStageBytes : exchange_bytes(splits));
   }
-  static constexpr int smem_bytes(int stages, int splits) {
-    return 1024 + ring_bytes(stages, splits) + kBarrierBytes;
+  static constexpr int smem_bytes(int stages, int splits, bool early) {
+    return 1024 + data_bytes(stages, splits, early) + kBarrierBytes;
   }
 };
 
@@ -72,15 +82,17 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int stages = args.stages;
-  uint8_t* ring = smem;  // after the main loop it holds this CTA's FP32 partial [MP][NT]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + S::ring_bytes(stages, args.splits));
+  const bool early = args.early != 0;
+  uint8_t* ring = smem;
+  uint8_t* exchange = early ? ring + stages * S::kStageBytes : ring;  // the S slots [MP][W]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + S::data_bytes(stages, args.splits, early));
   uint64_t* full = bars;
   uint64_t* empty = bars + kStreamMaxStages;
   uint64_t* tmem_full = bars + 2 * kStreamMaxStages;
   uint64_t* mma_done = tmem_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* recv_bar = mma_done + 1;  // bytes of the S slots this CTA owns the sum of
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* partial = reinterpret_cast<float*>(ring);
 
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = lane_id();
@@ -96,6 +108,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     }
     mbar_init(tmem_full, 1);
     mbar_init(mma_done, 1);
+    mbar_init(recv_bar, 1);
+    if (S::kAsyncPush && args.splits > 1) {
+      const int w = S::owner_cols(args.splits);
+      const int own_cols = min(w, S::kNT - split * w);
+      mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(args.splits * args.m * own_cols * 4));
+    }
     *abort_flag = 0;
     fence_mbarrier_init();
     tma_prefetch_map(&map_a);
@@ -108,6 +126,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
+  // Every CTA's receive barrier is armed before anyone pushes: the arrive here, the wait below.
+  if (args.splits > 1 && early) cluster_arrive_relaxed();
   const uint32_t tmem_base = *tmem_slot;
   bool have_result = false;
 
@@ -197,10 +217,16 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   const int splits = args.splits;
   const int cols = S::owner_cols(splits);            // columns of C each CTA of the cluster owns
   const int slot_bytes = MP * cols * 4;              // one source split's slice, FP32 [MP][cols]
-  const uint32_t base = smem_addr(partial);
-  if (splits > 1) cluster_sync();  // every main loop is done: all rings can receive
+  const uint32_t base = smem_addr(exchange);
+  if (splits > 1) {
+    if (early) {
+      cluster_wait();  // every receive barrier is armed
+    } else {
+      cluster_sync();  // every main loop is done: all rings can receive
+    }
+  }
   if (warp >= 2 && have_result) {
-    // ---- TMEM -> C (one split) or -> the owner's shared memory (remote stores) ----
+    // ---- TMEM -> C (one split) or -> the owner's slot (asynchronous stores, own one too) ----
     tc_fence_after_sync();
     const int quarter = warp & 3;
 #pragma unroll 1
@@ -211,6 +237,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       const uint32_t dst = splits > 1 ? map_to_rank(base + split * slot_bytes + (nl - owner * cols) * 4,
                                                     static_cast<uint32_t>(owner))
                                       : 0u;
+      const uint32_t owner_bar = splits > 1 ? map_to_rank(smem_addr(recv_bar), static_cast<uint32_t>(owner)) : 0u;
       const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * MP;
 #pragma unroll 1
       for (int c0 = 0; c0 < MP; c0 += kChunk) {
@@ -234,8 +261,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 #pragma unroll
           for (int j = 0; j < kChunk; ++j) {
             if (c0 + j < args.m) {
-              asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(dst + (c0 + j) * cols * 4), "r"(r[j])
-                           : "memory");
+              if constexpr (S::kAsyncPush) {
+                st_async_b32(dst + (c0 + j) * cols * 4, r[j], owner_bar);
+              } else {
+                st_dsmem_b32(dst + (c0 + j) * cols * 4, r[j]);
+              }
             }
           }
         }
@@ -244,14 +274,20 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   }
 
   if (splits > 1) {
-    cluster_sync();  // every slice has arrived
-    // ---- reduce locally in split order and write FP16 C ----
-    const int rank = static_cast<int>(cluster_ctarank());
+    // ---- wait for the S slots, reduce in split order and write FP16 C ----
+    bool arrived = true;
+    if constexpr (S::kAsyncPush) {
+      arrived = mbar_wait_cluster(recv_bar, 0, abort_flag);
+    } else {
+      cluster_sync();  // every slice has arrived
+    }
+    if (!arrived && threadIdx.x == 64) raise_abort(args.status, abort_flag, kStatusEpilogueTimeout);
+    const int rank = split;
     const int own_cols = min(cols, S::kNT - rank * cols);  // the last owner may have fewer
     const int quads = own_cols / 4;
     const int items = args.m * quads;
     const bool vec_store = (args.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(args.c) & 7) == 0);
-    for (int i = threadIdx.x; i < items; i += blockDim.x) {
+    for (int i = threadIdx.x; arrived && i < items; i += blockDim.x) {
       const int m = i / quads;
       const int q = i % quads;
       const uint32_t offset = static_cast<uint32_t>((m * cols + q * 4) * 4);

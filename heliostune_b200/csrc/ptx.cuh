@@ -365,6 +365,57 @@ __device__ __forceinline__ void st_global_v4(float* p, uint32_t a, uint32_t b, u
                : "memory");
 }
 
+// Asynchronous 4-byte store into (possibly another CTA's) shared memory; its bytes complete on
+// the mbarrier at `bar_cluster` in the same CTA as the destination.
+__device__ __forceinline__ void st_async_b32(uint32_t dst_cluster, uint32_t v, uint32_t bar_cluster) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(
+                   dst_cluster),
+               "r"(v), "r"(bar_cluster)
+               : "memory");
+}
+
+// 4-byte store into (possibly another CTA's) shared memory at a shared::cluster address.
+__device__ __forceinline__ void st_dsmem_b32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
+// mbar_wait with cluster-scope acquire: what other CTAs released into the barrier is visible.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i) {
+      if (mbar_try_wait_cluster(bar, parity)) return true;
+    }
+    if (abort != nullptr && *abort) return false;
+    if (global_timer_ns() - start > limit_ns) return false;
+  }
+}
+
+// The two halves of a cluster barrier: arrive without waiting (no memory ordering), and wait
+// (acquire) for every thread of the cluster to have arrived.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  __syncwarp();
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
+
 // Barrier among the `count` threads of named barrier `id` (the epilogue warps).
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
