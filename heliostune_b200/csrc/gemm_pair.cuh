@@ -19,11 +19,12 @@
 // S pairs compute the same 256 x BN tile over S contiguous K ranges. CTA (r, s) owns columns
 // [s*BN/S, (s+1)*BN/S) of its 128 rows. Once every CTA's main loop is done (cluster barrier, so
 // all rings are drained), each CTA stages the column slices it does not own from TMEM into its
-// own shared memory and sends each with one asynchronous bulk copy into the owner's receive
-// slot (completed in bytes on the owner's mbarrier). The owner then adds, in split order, its
-// own slice read straight from TMEM and the S - 1 received slices, and stores FP16 C through
-// the usual staged TMA-store epilogue. One tile per cluster; no workspace, no atomics, bitwise
-// reproducible.
+// own shared memory, 64 columns at a time, and sends each piece with one asynchronous bulk copy
+// into the owner's receive slot while it stages the next (completed in bytes on the owner's
+// mbarrier of that piece). The owner then adds, piece by piece as they arrive and in split
+// order, its own columns read straight from TMEM and the S - 1 received pieces, and stores FP16
+// C through the usual staged TMA-store epilogue. One tile per cluster; no workspace, no atomics,
+// bitwise reproducible.
 //
 // Stream-K (persistent mode with PairStreamKArgs::sk_tiles > 0), for tile counts that leave the
 // last wave of pairs part-empty: the first sk_tiles tiles are cut along K into one contiguous
@@ -166,8 +167,8 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   uint64_t* tmem_full = bars + 2 * kMaxStages;
   uint64_t* tmem_empty = tmem_full + 2;
   uint64_t* mma_done = tmem_empty + 2;
-  uint64_t* recv_bar = mma_done + 1;  // split mode: the S - 1 incoming slices
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
+  uint64_t* recv_bar = mma_done + 1;  // split mode: one per 64-column piece this CTA owns
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -201,11 +202,12 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       mbar_init(&tmem_empty[b], 8);  // four epilogue warps in each CTA (leader's copy is used)
     }
     mbar_init(mma_done, 1);
-    mbar_init(recv_bar, 1);
     if (SPLIT) {
-      // Armed before anyone can send: the phase completes once every incoming byte is here.
-      const int slice_bytes = 128 * (BN / split_args.splits) * 4;
-      mbar_arrive_expect_tx(recv_bar, (split_args.splits - 1) * slice_bytes);
+      // Armed before anyone can send: a piece's phase completes once all S - 1 copies are here.
+      for (int q = 0; q < BN / split_args.splits / 64; ++q) {
+        mbar_init(&recv_bar[q], 1);
+        mbar_arrive_expect_tx(&recv_bar[q], (split_args.splits - 1) * 128 * 64 * 4);
+      }
     }
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -555,106 +557,108 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   if constexpr (SPLIT) {
     const int splits = split_args.splits;
     const int cols = BN / splits;                 // columns each CTA owns (>= 64)
-    const int slice_bytes = 128 * cols * 4;       // one 128-row FP32 column slice
-    const int row_bytes = cols * 4;
-    uint8_t* outgoing = ring;                     // S - 1 slices this CTA sends
-    uint8_t* incoming = ring + (splits - 1) * slice_bytes;  // S - 1 slices it receives
+    const int pieces = cols / 64;                 // 64-column pieces of one slice
+    constexpr int kPieceBytes = 128 * 64 * 4;     // one 128-row FP32 piece, 256-byte rows
+    uint8_t* outgoing = ring;                     // the S - 1 slices this CTA sends
+    uint8_t* incoming = ring + (splits - 1) * pieces * kPieceBytes;  // the S - 1 it receives
     // Slot of split `src` among the S - 1 slices CTA `dst` exchanges (its own is never sent).
     auto slot_of = [](int src, int dst) { return src < dst ? src : src - 1; };
-    auto slot = [&](int other) { return slot_of(other, split); };
     cluster_sync();  // every main loop is done: all rings are free
     if (warp >= 2) {
       const int quarter = warp & 3;
       const uint32_t row = static_cast<uint32_t>(quarter * 32) + lane;
       const uint32_t lane_tmem = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-      if (split_ready) {
-        tc_fence_after_sync();
-        // ---- stage the slices other CTAs own ----
+      if (split_ready) tc_fence_after_sync();
+      // ---- send: stage each 64-column piece other CTAs own, then copy it while the next is
+      // staged; each piece completes on the owner's barrier of that piece ----
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          const int owner = c / cols;
-          if (owner == split) continue;
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(lane_tmem + c, v);
-          tmem_ld_wait();
-          const uint32_t dst = smem_addr(outgoing + slot(owner) * slice_bytes) + row * row_bytes;
-          const int local = c - owner * cols;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const uint32_t chunk = static_cast<uint32_t>(local / 4 + j);
-            st_shared_v4(dst + ((chunk ^ (row & 7u)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
-                         v[4 * j + 3]);
-          }
-        }
-      }
-      fence_proxy_async_smem();
-      named_barrier(1, 128);
-      if (warp == 2 && lane == 0) {
-        for (int owner = 0; owner < splits; ++owner) {
-          if (owner == split) continue;
-          const uint32_t owner_rank = rank + 2u * static_cast<uint32_t>(owner);
-          bulk_copy_to_cluster(map_to_rank(smem_addr(incoming + slot_of(split, owner) * slice_bytes), owner_rank),
-                               outgoing + slot(owner) * slice_bytes, static_cast<uint32_t>(slice_bytes),
-                               map_to_rank(smem_addr(recv_bar), owner_rank));
-        }
-      }
-      // ---- wait for the S - 1 slices this CTA owns the sum of ----
-      const bool arrived = __all_sync(0xffffffffu, mbar_wait(recv_bar, 0, abort_flag));
-      if (!arrived && lane == 0) raise_abort(args.status, abort_flag, kStatusEpilogueTimeout);
-      if (split_ready && arrived) {
-        int pm, pn;
-        grouped_tile(pair, args.tiles_m, args.tiles_n, args.group_m, pm, pn);
-        const int row0 = pm * 256 + static_cast<int>(rank) * 128 + quarter * 32;
-        uint8_t* staging = epi + (warp - 2) * 2 * kEpilogueStageBytes;
-        int buf = 0;
+      for (int owner = 0; owner < splits; ++owner) {
+        if (owner == split) continue;
+        const uint32_t owner_rank = rank + 2u * static_cast<uint32_t>(owner);
 #pragma unroll 1
-        for (int c = 0; c < cols; c += 64) {
-          uint32_t own[64];
-          tmem_ld_32x32b_x32(lane_tmem + split * cols + c, *reinterpret_cast<uint32_t(*)[32]>(own));
-          tmem_ld_32x32b_x32(lane_tmem + split * cols + c + 32, *reinterpret_cast<uint32_t(*)[32]>(own + 32));
-          tmem_ld_wait();
-          float acc[64];
+        for (int q = 0; q < pieces; ++q) {
+          uint8_t* piece = outgoing + (slot_of(owner, split) * pieces + q) * kPieceBytes;
+          if (split_ready) {
+            uint32_t v[32];
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+              tmem_ld_32x32b_x32(lane_tmem + owner * cols + q * 64 + h * 32, v);
+              tmem_ld_wait();
+              const uint32_t dst = smem_addr(piece) + row * 256;
 #pragma unroll
-          for (int j = 0; j < 64; ++j) acc[j] = 0.f;
-          for (int src = 0; src < splits; ++src) {  // split order
-            if (src == split) {
-#pragma unroll
-              for (int j = 0; j < 64; ++j) acc[j] = src == 0 ? __uint_as_float(own[j]) : acc[j] + __uint_as_float(own[j]);
-            } else {
-              const uint32_t base_addr = smem_addr(incoming + slot(src) * slice_bytes) + row * row_bytes;
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const uint32_t chunk = static_cast<uint32_t>(c / 4 + j);
-                const float4 v = ld_shared_f32x4(base_addr + ((chunk ^ (row & 7u)) << 4));
-                if (src == 0) {
-                  acc[4 * j] = v.x; acc[4 * j + 1] = v.y; acc[4 * j + 2] = v.z; acc[4 * j + 3] = v.w;
-                } else {
-                  acc[4 * j] += v.x; acc[4 * j + 1] += v.y; acc[4 * j + 2] += v.z; acc[4 * j + 3] += v.w;
-                }
+              for (int j = 0; j < 8; ++j) {
+                const uint32_t chunk = static_cast<uint32_t>(h * 8 + j);
+                st_shared_v4(dst + ((chunk ^ (row & 7u)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                             v[4 * j + 3]);
               }
             }
           }
-          uint8_t* dst = staging + buf * kEpilogueStageBytes;
-          if (lane == 0) bulk_wait_group_read<1>();
-          __syncwarp();
-          const uint32_t row_addr = smem_addr(dst) + lane * 128;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), pack_half2(acc[8 * j], acc[8 * j + 1]),
-                         pack_half2(acc[8 * j + 2], acc[8 * j + 3]), pack_half2(acc[8 * j + 4], acc[8 * j + 5]),
-                         pack_half2(acc[8 * j + 6], acc[8 * j + 7]));
-          }
           fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&map_c, dst, pn * BN + split * cols + c, row0);
-            bulk_commit_group();
+          named_barrier(1, 128);
+          if (warp == 2 && lane == 0 && split_ready) {
+            bulk_copy_to_cluster(
+                map_to_rank(smem_addr(incoming + (slot_of(split, owner) * pieces + q) * kPieceBytes), owner_rank),
+                piece, static_cast<uint32_t>(kPieceBytes), map_to_rank(smem_addr(&recv_bar[q]), owner_rank));
           }
-          buf ^= 1;
         }
-        if (lane == 0) bulk_wait_group<0>();
-        __syncwarp();
       }
+      // ---- receive: each owned piece as soon as its S - 1 copies are here ----
+      int pm, pn;
+      grouped_tile(pair, args.tiles_m, args.tiles_n, args.group_m, pm, pn);
+      const int row0 = pm * 256 + static_cast<int>(rank) * 128 + quarter * 32;
+      uint8_t* staging = epi + (warp - 2) * 2 * kEpilogueStageBytes;
+      int buf = 0;
+#pragma unroll 1
+      for (int q = 0; q < pieces; ++q) {
+        const bool arrived = __all_sync(0xffffffffu, mbar_wait(&recv_bar[q], 0, abort_flag));
+        if (!arrived && lane == 0) raise_abort(args.status, abort_flag, kStatusEpilogueTimeout);
+        if (!split_ready || !arrived) break;
+        const int c = q * 64;
+        uint32_t own[64];
+        tmem_ld_32x32b_x32(lane_tmem + split * cols + c, *reinterpret_cast<uint32_t(*)[32]>(own));
+        tmem_ld_32x32b_x32(lane_tmem + split * cols + c + 32, *reinterpret_cast<uint32_t(*)[32]>(own + 32));
+        tmem_ld_wait();
+        float acc[64];
+#pragma unroll
+        for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+        for (int src = 0; src < splits; ++src) {  // split order
+          if (src == split) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) acc[j] = src == 0 ? __uint_as_float(own[j]) : acc[j] + __uint_as_float(own[j]);
+          } else {
+            const uint32_t base_addr =
+                smem_addr(incoming + (slot_of(src, split) * pieces + q) * kPieceBytes) + row * 256;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float4 v = ld_shared_f32x4(base_addr + ((static_cast<uint32_t>(j) ^ (row & 7u)) << 4));
+              if (src == 0) {
+                acc[4 * j] = v.x; acc[4 * j + 1] = v.y; acc[4 * j + 2] = v.z; acc[4 * j + 3] = v.w;
+              } else {
+                acc[4 * j] += v.x; acc[4 * j + 1] += v.y; acc[4 * j + 2] += v.z; acc[4 * j + 3] += v.w;
+              }
+            }
+          }
+        }
+        uint8_t* dst = staging + buf * kEpilogueStageBytes;
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        const uint32_t row_addr = smem_addr(dst) + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), pack_half2(acc[8 * j], acc[8 * j + 1]),
+                       pack_half2(acc[8 * j + 2], acc[8 * j + 3]), pack_half2(acc[8 * j + 4], acc[8 * j + 5]),
+                       pack_half2(acc[8 * j + 6], acc[8 * j + 7]));
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&map_c, dst, pn * BN + split * cols + c, row0);
+          bulk_commit_group();
+        }
+        buf ^= 1;
+      }
+      if (lane == 0) bulk_wait_group<0>();
+      __syncwarp();
     }
   }
 
