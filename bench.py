@@ -454,7 +454,7 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
     import torch.distributed as dist
 
     from heliostune_b200 import _native
-    from heliostune_b200.column_parallel import COLUMN_PARALLEL_CANDIDATE, ColumnShard, column_parallel_matmul
+    from heliostune_b200.column_parallel import ColumnShard, column_parallel_candidate, column_parallel_matmul
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -535,7 +535,7 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
         "config": {
             "workload": f"colpar M={w.m} N={w.n} K={w.k}",
             "parallelism": f"column-parallel x{world}",
-            "gemm": COLUMN_PARALLEL_CANDIDATE.key,
+            "gemm": column_parallel_candidate(w.m, shard.cols).key,
             "l2": "operands larger than L2",
         },
         "gemm_ms": round(gemm_ms, 4),

@@ -1047,6 +1047,7 @@ int hst_matmul_pair_fanout(int32_t block_n, int32_t block_k, int32_t num_stages,
   if (p.bn == 128 && p.bk == 64) return launch_pair<128, 64, false>(*dev, o, p.stages, p.group_m, 1, 0, s, &fanout);
   if (p.bn == 256 && p.bk == 128) return launch_pair<256, 128, false>(*dev, o, p.stages, p.group_m, 1, 0, s, &fanout);
   if (p.bn == 128 && p.bk == 128) return launch_pair<128, 128, false>(*dev, o, p.stages, p.group_m, 1, 0, s, &fanout);
+  if (p.bn == 512 && p.bk == 64) return launch_pair<512, 64, false>(*dev, o, p.stages, p.group_m, 1, 0, s, &fanout);
   return fail(HST_ERR_UNSUPPORTED, "no pair kernel for N %d, K %d", p.bn, p.bk);
 }
 

@@ -105,16 +105,26 @@ def _fused_rank(rank: int, world: int, port: int, queue) -> None:  # type: ignor
     torch.cuda.set_device(rank)
     device = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=device)
+    from heliostune_b200.action_expansion import launch
+    from heliostune_b200.column_parallel import COLUMN_PARALLEL_CANDIDATE, COLUMN_PARALLEL_WIDE
+
     try:
         results = []
-        for m, k, n in ((1000, 1032, 2 * 1024), (512, 4096, 2 * 1536)):
+        cases = (
+            (1000, 1032, 2 * 1024, None),
+            (512, 4096, 2 * 1536, None),
+            (1000, 520, 2 * 1280, COLUMN_PARALLEL_WIDE),  # 256 x 512 tiles, ragged last tile
+            (600, 1024, 2 * 3072, COLUMN_PARALLEL_CANDIDATE),
+        )
+        for m, k, n, candidate in cases:
             g = torch.Generator(device=device).manual_seed(m + k)
             a = (torch.randn((m, k), generator=g, device=device) / k**0.5).to(torch.float16)
             b = (torch.randn((k, n), generator=g, device=device) / k**0.5).to(torch.float16)
             shard = ColumnShard(n, world, rank)
-            fused = FusedColumnParallel(m, n, device=device)
+            fused = FusedColumnParallel(m, n, device=device, candidate=candidate)
             expected = fp32_reference(a, b)
-            plain = column_parallel_matmul(a, shard.take(b))
+            gemm = None if candidate is None else (lambda x, y, c=candidate: launch(x, y, c))
+            plain = column_parallel_matmul(a, shard.take(b), gemm=gemm)
             for _ in range(2):  # the second call reuses the mapped outputs
                 c = fused(a, shard.take(b)).clone()
                 close = bool(torch.allclose(c.float(), expected, atol=1e-2, rtol=1e-2))
