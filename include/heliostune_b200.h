@@ -105,9 +105,9 @@ int hst_matmul_split_k(int32_t block_m, int32_t block_n, int32_t block_k, int32_
                        size_t workspace_bytes, void* stream);
 
 /* B200 weight-streaming family (no reference counterpart): 1 <= m <= 256, block_n 128 or 256
- * columns of C per CTA (256 needs block_m 64 or 128). split_k (1, 2, 4 or 8; 0 = the largest that
- * fills one wave) CTAs form a cluster whose partials are summed in split order through
- * distributed shared memory: no workspace for aligned operands. */
+ * columns of C per CTA (256 needs block_m 64 or 128). split_k (1..8; 0 = the count putting the
+ * most CTAs in one resident wave) CTAs form a cluster whose partials are summed in split order
+ * through distributed shared memory: no workspace for aligned operands. */
 int hst_matmul_stream(int32_t block_m, int32_t block_n, int32_t block_k, int32_t num_stages,
                       int32_t split_k,
                       const void* a, int64_t a_stride0, int64_t a_stride1, const void* b,
@@ -116,8 +116,9 @@ int hst_matmul_stream(int32_t block_m, int32_t block_n, int32_t block_k, int32_t
                       void* stream);
 
 /* B200 CTA-pair family (no reference counterpart): clusters of two CTAs computing 256 x block_n
- * tiles (block_n 128 or 256) with tcgen05.mma.cta_group::2, persistent over the tiles. split_k
- * 2 or 4 (0 = automatic when the tiles leave most SMs idle) makes clusters of 2 x split_k CTAs
+ * tiles (block_n 128, 256, or 512 with block_k 64) with tcgen05.mma.cta_group::2, persistent over
+ * the tiles. split_k 2 or 4 (block_n 128 or 256; 0 = automatic when the tiles leave most SMs
+ * idle) makes clusters of 2 x split_k CTAs
  * that divide K and sum their partials in split order through distributed shared memory.
  * split_k HST_PAIR_STREAM_K balances a part-filled last wave: the tiles
  * hst_pair_stream_k_tiles names are cut along K into one equal run of K blocks per pair, the
