@@ -547,7 +547,7 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
             "unit": "TFLOP/s",
             "frac": round(gemm_tflops / peaks["bf16_tflops_sustained"], 4),
             "peak_source": f"{source} (sustained)",
-            "kernel": "pair_gemm_kernel<256,64> (GEMM phase, per GPU)",
+            "kernel": f"pair_gemm_kernel<{column_parallel_candidate(w.m, shard.cols).config.block_n},64> (GEMM phase, per GPU)",
             "traffic": None,
         },
         "step_roofline_frac": round(t_roof / (step_ms / 1e3), 4),
