@@ -64,6 +64,7 @@ EXPORTED_SYMBOLS = (
     "hst_ipc_import",
     "hst_ipc_close",
     "hst_pair_stream_k_tiles",
+    "hst_rmsnorm_matmul_stream",
 )
 
 
@@ -139,6 +140,10 @@ def _declare(lib: ctypes.CDLL) -> None:
             ctypes.c_int,
         ),
         "hst_pair_stream_k_tiles": ([_i64, _i64, _i64, ctypes.POINTER(_i64)], ctypes.c_int),
+        "hst_rmsnorm_matmul_stream": (
+            [_i32] * 5 + [_ptr, _i64, _ptr, ctypes.c_float, _ptr, _i64, _ptr, _i64, _i64, _i64, _i64, _ptr],
+            ctypes.c_int,
+        ),
         "hst_matmul_pair": (
             [_i32] * 5 + [_ptr, _i64, _i64, _ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i64,
                           _ptr, _size, _ptr],

@@ -715,9 +715,15 @@ int dispatch_stream(const DeviceState& dev, const Plan& p, const Operands& o, fl
               p.bk);
 }
 
+// RMSNorm prologue of the stream family: gamma [k] (null = plain GEMM) and eps.
+struct RowNorm {
+  const __half* gamma = nullptr;
+  float eps = 0.f;
+};
+
 template <int NA, int MP, int BK>
 int launch_stream_cluster(const DeviceState& dev, const Operands& o, int stages, int splits,
-                          int kb_per_split, cudaStream_t stream) {
+                          int kb_per_split, cudaStream_t stream, const RowNorm& norm = RowNorm{}) {
   using S = ClusterStreamShape<NA, MP, BK>;
   static std::atomic<uint64_t> smem_done{0};
   HST_TRY(allow_smem(stream_cluster_kernel<NA, MP, BK>, smem_done));
@@ -741,6 +747,9 @@ int launch_stream_cluster(const DeviceState& dev, const Operands& o, int stages,
   args.splits = splits;
   args.stages = stages;
   args.early = early ? 1 : 0;
+  args.norm = norm.gamma != nullptr ? 1 : 0;
+  args.eps = norm.eps;
+  args.gamma = norm.gamma;
   args.status = dev.status;
   args.c = o.c;
   args.ldc = o.ldc;
@@ -761,11 +770,11 @@ int launch_stream_cluster(const DeviceState& dev, const Operands& o, int stages,
 }
 
 int dispatch_stream_cluster(const DeviceState& dev, const Plan& p, const Operands& o,
-                            cudaStream_t stream) {
+                            cudaStream_t stream, const RowNorm& norm = RowNorm{}) {
 #define HST_CLUSTER_CASE(NA_, MP_, BK_)                                                   \
   if (p.nt == 128 * NA_ && p.mp == MP_ && p.bk == BK_)                                    \
     return launch_stream_cluster<NA_, MP_, BK_>(dev, o, p.stages, p.splits, p.kb_per_split, \
-                                                stream);
+                                                stream, norm);
   HST_CLUSTER_CASE(1, 16, 64)
   HST_CLUSTER_CASE(1, 32, 64)
   HST_CLUSTER_CASE(1, 64, 64)
@@ -988,6 +997,41 @@ int hst_matmul_stream(int32_t block_m, int32_t block_n, int32_t block_k, int32_t
   const hst_gemm_config cfg{HST_FAMILY_STREAM, block_m, block_n, block_k, 4, num_stages, 8, split_k};
   return gemm_impl(&cfg, a, a_stride0, a_stride1, b, b_stride0, b_stride1, c, ldc, m, n, k,
                    workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int hst_rmsnorm_matmul_stream(int32_t block_m, int32_t block_n, int32_t block_k,
+                              int32_t num_stages, int32_t split_k, const void* x, int64_t ldx,
+                              const void* gamma, float eps, const void* w, int64_t ldw, void* c,
+                              int64_t ldc, int64_t m, int64_t n, int64_t k, void* stream) {
+  HST_TRY(check_problem(x, w, c, m, n, k, ldc));
+  if (gamma == nullptr) return fail(HST_ERR_INVALID, "gamma is null");
+  if (block_m > 128) return fail(HST_ERR_UNSUPPORTED, "the RMSNorm prologue needs block_m <= 128");
+  if (k % 8 != 0 || (reinterpret_cast<uintptr_t>(gamma) & 15) != 0)
+    return fail(HST_ERR_INVALID, "the RMSNorm prologue needs K %% 8 == 0 and a 16-byte aligned gamma");
+  DeviceState* dev = nullptr;
+  HST_TRY(device_state(&dev));
+  const hst_gemm_config cfg{HST_FAMILY_STREAM, block_m, block_n, block_k, 4, num_stages, 8, split_k};
+  const View vx{static_cast<const __half*>(x), m, k, m > 1 ? ldx : k, 1};
+  const View vw{static_cast<const __half*>(w), k, n, ldw, 1};
+  Plan p;
+  HST_TRY(make_plan(&cfg, vx, vw, m, n, k, dev->sm_count, &p));
+  if (p.pack_a || p.pack_b)
+    return fail(HST_ERR_INVALID, "x and W must be row-major with 16-byte aligned rows");
+  if (m == 0 || n == 0) return HST_OK;
+  Operands o;
+  o.m = static_cast<int>(m);
+  o.n = static_cast<int>(n);
+  o.k = static_cast<int>(k);
+  o.a = vx.ptr;
+  o.lda = tma_row_stride(vx);
+  o.b = vw.ptr;
+  o.ldb = tma_row_stride(vw);
+  o.c = static_cast<__half*>(c);
+  o.ldc = ldc;
+  RowNorm norm;
+  norm.gamma = static_cast<const __half*>(gamma);
+  norm.eps = eps;
+  return dispatch_stream_cluster(*dev, p, o, static_cast<cudaStream_t>(stream), norm);
 }
 
 int hst_matmul_pair(int32_t block_n, int32_t block_k, int32_t num_stages, int32_t group_m,

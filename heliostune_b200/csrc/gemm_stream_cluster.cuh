@@ -19,6 +19,12 @@
 //         (cheaper per byte than the asynchronous stores once each thread sends 128 words).
 //     No workspace, no second kernel, no atomics; the result is bitwise reproducible.
 // With S = 1 the epilogue writes C straight from TMEM.
+//
+// RMSNorm prologue (args.norm): C = RMSNorm(A; gamma, eps) * B for an unnormalised A. While the
+// main loop runs, the four epilogue warps take every A^T tile as it lands, add its squares to
+// per-row FP32 sums and rewrite it in place as fp16(a * gamma[k]); the UMMAs wait for that
+// (a second barrier per stage). The row factors rsqrt(sum / K + eps) are applied to the FP32
+// results in the epilogue, after the per-split sums have crossed the cluster with the slices.
 #pragma once
 
 #include "ptx.cuh"
@@ -32,6 +38,9 @@ struct ClusterStreamArgs {
   int splits;  // cluster size along y
   int stages;
   int early;   // exchange slots beside the ring (1) or in it after the main loops (0)
+  int norm;    // RMSNorm prologue on A (see the file comment)
+  float eps;
+  const __half* gamma;  // [k] when norm
   int* status;
   __half* c;
   int64_t ldc;
@@ -54,9 +63,9 @@ struct ClusterStreamShape {
   __host__ __device__ static constexpr int owner_cols(int splits) {
     return ((kNT + splits - 1) / splits + 3) / 4 * 4;
   }
-  // The S exchange slots, [MP][owner_cols] FP32 each.
+  // The S exchange slots, [MP][owner_cols] FP32 each, then S row-sum slots of MP floats.
   __host__ __device__ static constexpr int exchange_bytes(int splits) {
-    return splits * owner_cols(splits) * MP * 4;
+    return splits * owner_cols(splits) * MP * 4 + splits * MP * 4;
   }
   static constexpr int kCols = NA * MP;
   static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128 : kCols <= 256 ? 256 : 512;
@@ -91,7 +100,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   uint64_t* tmem_full = bars + 2 * kStreamMaxStages;
   uint64_t* mma_done = tmem_full + 1;
   uint64_t* recv_bar = mma_done + 1;  // bytes of the S slots this CTA owns the sum of
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
+  uint64_t* scaled = recv_bar + 1;    // RMSNorm prologue: stage rewritten by the epilogue warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(scaled + kStreamMaxStages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -105,6 +115,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&scaled[s], 4);
     }
     mbar_init(tmem_full, 1);
     mbar_init(mma_done, 1);
@@ -112,7 +123,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     if (S::kAsyncPush && args.splits > 1) {
       const int w = S::owner_cols(args.splits);
       const int own_cols = min(w, S::kNT - split * w);
-      mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(args.splits * args.m * own_cols * 4));
+      const int sums = args.norm ? args.m : 0;  // the row sums travel with the slices
+      mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(args.splits * (args.m * own_cols + sums) * 4));
     }
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -130,6 +142,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   if (args.splits > 1 && early) cluster_arrive_relaxed();
   const uint32_t tmem_base = *tmem_slot;
   bool have_result = false;
+  constexpr int kTpr = MP >= 128 ? 1 : 128 / MP;  // RMSNorm prologue: threads per row
+  float row_ss = 0.f;                            // this thread's part of its row's sum of squares
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
@@ -178,7 +192,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     uint32_t phase = 0;
     bool ok = true;
     for (int kb = kb_begin; kb < kb_end; ++kb) {
-      if (!mbar_wait(&full[stage], phase, abort_flag)) {
+      if (!mbar_wait(args.norm ? &scaled[stage] : &full[stage], phase, abort_flag)) {
         raise_abort(args.status, abort_flag, kStatusMmaTimeout);
         ok = false;
         break;
@@ -208,6 +222,56 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     umma_commit(mma_done);
     if (!mbar_wait(mma_done, 0, nullptr, 200000000ull)) atomicOr(args.status, kStatusDrainTimeout);
   } else if (warp >= 2) {
+    if (args.norm) {
+      // ---------------- RMSNorm prologue: sum of squares and gamma on every A^T tile ----------
+      // Thread t owns row t / kTpr of the tile and every kTpr-th 16-byte chunk of that row.
+      const int t = threadIdx.x - 64;
+      const int row = t / kTpr;
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb_begin; kb < kb_end && ok; ++kb) {
+        ok = mbar_wait(&full[stage], phase, abort_flag);
+        if (!ok) {
+          if (lane == 0) raise_abort(args.status, abort_flag, kStatusEpilogueTimeout);
+          break;
+        }
+        const uint32_t x_base = smem_addr(ring + stage * S::kStageBytes + S::kWBytes);
+        if (row < MP) {
+#pragma unroll 1
+          for (int ka = 0; ka < S::kAtomsK; ++ka) {
+            const uint32_t row_addr = x_base + ka * S::kXBoxBytes + row * 128;
+            for (int p = t % kTpr; p < 8; p += kTpr) {
+              const uint32_t addr = row_addr + (static_cast<uint32_t>(p) << 4);
+              const int k = kb * BK + ka * 64 + ((p ^ (row & 7)) << 3);  // swizzled chunk position
+              float4 raw = ld_shared_f32x4(addr);
+              __half* h = reinterpret_cast<__half*>(&raw);
+              uint4 g = make_uint4(0, 0, 0, 0);
+              if (k < args.k) g = *reinterpret_cast<const uint4*>(args.gamma + k);
+              const __half* gh = reinterpret_cast<const __half*>(&g);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float v = __half2float(h[e]);
+                row_ss = fmaf(v, v, row_ss);
+                h[e] = __float2half_rn(v * __half2float(gh[e]));
+              }
+              const uint32_t* w = reinterpret_cast<const uint32_t*>(&raw);
+              st_shared_v4(addr, w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+        fence_proxy_async_smem();  // the rewritten tile is visible to the UMMAs
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&scaled[stage]);
+        if (++stage == stages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      // One partial sum per row for this CTA's K range: the row's kTpr threads are neighbours.
+#pragma unroll
+      for (int off = 1; off < kTpr; off <<= 1) row_ss += __shfl_xor_sync(0xffffffffu, row_ss, off);
+    }
     // ---------------- epilogue: wait for the accumulator ----------------
     have_result = __all_sync(0xffffffffu, mbar_wait(tmem_full, 0, abort_flag));
     if (!have_result && lane == 0) raise_abort(args.status, abort_flag, kStatusEpilogueTimeout);
@@ -224,6 +288,36 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     } else {
       cluster_sync();  // every main loop is done: all rings can receive
     }
+  }
+  const uint32_t sums = base + splits * slot_bytes;  // RMSNorm row sums: [split][MP] FP32
+  auto row_factor = [&](int m) {  // rsqrt(mean of squares + eps) of row m, split order
+    float ss = 0.f;
+    for (int s2 = 0; s2 < splits; ++s2) {
+      float v;
+      asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(sums + (s2 * MP + m) * 4) : "memory");
+      ss = s2 == 0 ? v : ss + v;
+    }
+    return rsqrtf(ss / static_cast<float>(args.k) + args.eps);
+  };
+  if (warp >= 2 && args.norm) {
+    // ---- this CTA's row sums to every owner (with the slices), or to its own table ----
+    const int t = threadIdx.x - 64;
+    const int row = t / kTpr;
+    if (have_result && t % kTpr == 0 && row < args.m) {
+      if (splits == 1) {
+        asm volatile("st.shared.f32 [%0], %1;" ::"r"(sums + row * 4), "f"(row_ss) : "memory");
+      } else {
+        for (int owner = 0; owner < splits; ++owner) {
+          const uint32_t dst = map_to_rank(sums + (split * MP + row) * 4, static_cast<uint32_t>(owner));
+          if constexpr (S::kAsyncPush) {
+            st_async_b32(dst, __float_as_uint(row_ss), map_to_rank(smem_addr(recv_bar), static_cast<uint32_t>(owner)));
+          } else {
+            st_dsmem_b32(dst, __float_as_uint(row_ss));
+          }
+        }
+      }
+    }
+    if (splits == 1) named_barrier(1, 128);  // every row sum is in the table (all four warps)
   }
   if (warp >= 2 && have_result) {
     // ---- TMEM -> C (one split) or -> the owner's slot (asynchronous stores, own one too) ----
@@ -254,7 +348,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 #pragma unroll
             for (int j = 0; j < kChunk; ++j) {
               const int m = c0 + j;
-              if (m < args.m) args.c[static_cast<int64_t>(m) * args.ldc + n] = __float2half_rn(__uint_as_float(r[j]));
+              if (m < args.m) {
+                const float v = __uint_as_float(r[j]) * (args.norm ? row_factor(m) : 1.f);
+                args.c[static_cast<int64_t>(m) * args.ldc + n] = __float2half_rn(v);
+              }
             }
           }
         } else {
@@ -298,6 +395,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         acc.y += v.y;
         acc.z += v.z;
         acc.w += v.w;
+      }
+      if (args.norm) {
+        const float f = row_factor(m);
+        acc.x *= f;
+        acc.y *= f;
+        acc.z *= f;
+        acc.w *= f;
       }
       const int n = n0 + rank * cols + q * 4;
       __half* dst = args.c + static_cast<int64_t>(m) * args.ldc + n;

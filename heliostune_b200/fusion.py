@@ -56,22 +56,74 @@ def rmsnorm_matmul(
     w: torch.Tensor,
     candidate: ActionCandidate,
     eps: float = DEFAULT_EPS,
+    *,
+    fused: bool | None = None,
 ) -> torch.Tensor:
     """``RMSNorm(x; gamma, eps) @ W`` -- the RMSNorm feeding the QKV projection.
 
-    The normalised rows are produced exactly as the reference's formula rounds them,
-    ``fp16((x * rsqrt(mean(x^2) + eps)) * gamma)``, into a per-call workspace by the RMSNorm
-    kernel, and the GEMM candidate consumes that workspace on the same stream. Materialising the
-    ``[M, K]`` FP16 rows costs ``4MK`` bytes of HBM traffic (write + read) next to the GEMM's
-    ``2(MK + KN + MN)``; rescaling the A tiles inside the GEMM instead would put the same work
-    on the shared-memory path the tensor-core main loop is limited by.
+    Fused (weight-streaming candidates with ``block_m <= 128``, the default where it applies):
+    one launch of ``hst_rmsnorm_matmul_stream``, whose main loop rescales each x tile it loads by
+    gamma and sums the squares of its rows, and whose epilogue multiplies the FP32 results by
+    ``rsqrt(mean(x^2) + eps)`` -- no normalised copy of x, no second kernel. The products are
+    rounded once, after the row factor, instead of the reference's intermediate FP16 rows.
+
+    Unfused (any other candidate, or ``fused=False``): the normalised rows are produced exactly as
+    the reference's formula rounds them, ``fp16((x * rsqrt(mean(x^2) + eps)) * gamma)``, by the
+    RMSNorm kernel into a per-call buffer that the GEMM candidate then consumes on the same stream.
     """
+    from heliostune_b200.action_configs import StreamConfig
     from heliostune_b200.action_expansion import launch
 
     if w.ndim != 2 or w.shape[0] != x.shape[1]:
         raise ValueError(f"incompatible shapes: x {tuple(x.shape)} and W {tuple(w.shape)}")
-    normalised = rmsnorm(x, gamma, eps)
-    return launch(normalised, w, candidate)
+    config = candidate.config
+    can_fuse = (
+        isinstance(config, StreamConfig)
+        and config.block_m <= 128
+        and x.shape[0] <= config.block_m
+        and x.shape[1] % 8 == 0
+        and x.stride(1) == 1
+        and (x.shape[0] == 1 or x.stride(0) % 8 == 0)
+        and x.data_ptr() % 16 == 0
+        and w.is_contiguous()
+        and w.shape[1] % 8 == 0
+        and gamma.is_contiguous()
+        and gamma.data_ptr() % 16 == 0
+        and x.dtype == w.dtype == gamma.dtype == torch.float16
+        and x.device == w.device == gamma.device
+    )
+    if fused is None:
+        fused = can_fuse
+    elif fused and not can_fuse:
+        raise ValueError("the fused RMSNorm GEMM needs a stream candidate with block_m <= 128 and aligned row-major operands")
+    if not fused:
+        return launch(rmsnorm(x, gamma, eps), w, candidate)
+    m, k = int(x.shape[0]), int(x.shape[1])
+    n = int(w.shape[1])
+    out = torch.empty((m, n), device=x.device, dtype=torch.float16)
+    with torch.cuda.device(x.device):
+        _native.check(
+            _native.library().hst_rmsnorm_matmul_stream(
+                config.block_m,
+                config.block_n,
+                config.block_k,
+                config.num_stages,
+                config.split_k,
+                x.data_ptr(),
+                x.stride(0) if m > 1 else k,
+                gamma.data_ptr(),
+                float(eps),
+                w.data_ptr(),
+                n,
+                out.data_ptr(),
+                n,
+                m,
+                n,
+                k,
+                _stream(x.device),
+            )
+        )
+    return out
 
 
 RMSNORM_ENTRYPOINTS: tuple[str, ...] = ("heliostune_b200::rmsnorm",)

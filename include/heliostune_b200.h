@@ -131,6 +131,17 @@ int hst_matmul_pair(int32_t block_n, int32_t block_k, int32_t num_stages, int32_
                     int64_t b_stride0, int64_t b_stride1, void* c, int64_t ldc, int64_t m,
                     int64_t n, int64_t k, void* workspace, size_t workspace_bytes, void* stream);
 
+/* RMSNorm(x; gamma, eps) @ W with the normalisation inside the weight-streaming GEMM (no
+ * reference counterpart: the reference runs its RMSNorm op, _fusion_gpu.py:76, then the GEMM).
+ * While the main loop streams W, the GEMM rescales each x tile it loads by gamma and sums the
+ * squares of its rows; the FP32 results are multiplied by rsqrt(sum / k + eps) per row. Same
+ * tiles and split_k as hst_matmul_stream, block_m <= 128; x [m, k] and W [k, n] row-major with
+ * 16-byte aligned rows, k % 8 == 0, gamma [k] 16-byte aligned. x is read, never written. */
+int hst_rmsnorm_matmul_stream(int32_t block_m, int32_t block_n, int32_t block_k,
+                              int32_t num_stages, int32_t split_k, const void* x, int64_t ldx,
+                              const void* gamma, float eps, const void* w, int64_t ldw, void* c,
+                              int64_t ldc, int64_t m, int64_t n, int64_t k, void* stream);
+
 /* Host-only planning query of the stream-K schedule: how many of `tiles` pair tiles (each
  * k_blocks K blocks deep) are shared out along K over `pairs` persistent pairs (0 = none). */
 int hst_pair_stream_k_tiles(int64_t tiles, int64_t k_blocks, int64_t pairs, int64_t* sk_tiles);

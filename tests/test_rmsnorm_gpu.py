@@ -77,3 +77,47 @@ def test_registry_is_closed() -> None:
     assert load_rmsnorm("heliostune_b200::rmsnorm") is rmsnorm
     with pytest.raises(KeyError):
         load_rmsnorm("heliostune_fusion_v2::residual_rmsnorm_w4")
+
+
+@pytest.mark.parametrize("rows", (1, 7, 16, 31, 64, 100, 128))
+@pytest.mark.parametrize("split", (0, 1, 3, 4))
+@pytest.mark.parametrize("nk", ((6144, 4096), (1000, 1000)), ids=lambda s: f"n{s[0]}k{s[1]}")
+def test_rmsnorm_prologue_inside_the_stream_gemm(rows: int, split: int, nk: tuple[int, int]) -> None:
+    """The fused kernel against the FP32 formula: the row factor applied after the GEMM."""
+    from heliostune_b200.action_configs import ActionCandidate, StreamConfig, stream_block_m
+    from heliostune_b200.action_expansion import fp32_reference
+    from heliostune_b200.fusion import rmsnorm_matmul
+
+    n, k = nk
+    x, gamma = _inputs(rows, k, seed=rows * 7 + split)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    w = (torch.randn((k, n), generator=g, device="cuda") / k**0.5).to(torch.float16)
+    x0 = x.clone()
+    xf = x.float()
+    exact = fp32_reference(xf * torch.rsqrt((xf * xf).mean(dim=-1, keepdim=True) + 1e-6) * gamma.float(), w.float())
+    bm = stream_block_m(rows)
+    for block_n, block_k in ((128, 64), (128, 128), (256, 64)):
+        if block_n == 256 and bm not in (64, 128):
+            continue
+        candidate = ActionCandidate(StreamConfig(bm, block_n, block_k, 4, 4, split))
+        out = rmsnorm_matmul(x, gamma, w, candidate, 1e-6, fused=True)
+        err = (out.float() - exact).abs()
+        assert bool(torch.all(err <= 1e-2 + 1e-2 * exact.abs())), (block_n, block_k, err.max().item())
+        assert err.max().item() <= 1e-2 * exact.abs().max().item()
+        assert torch.equal(out.view(torch.int16), rmsnorm_matmul(x, gamma, w, candidate, 1e-6, fused=True).view(torch.int16))
+        unfused = rmsnorm_matmul(x, gamma, w, candidate, 1e-6, fused=False)
+        assert (out.float() - unfused.float()).abs().max().item() <= 1e-2 * exact.abs().max().item()
+    assert torch.equal(x.view(torch.int16), x0.view(torch.int16))
+
+
+def test_rmsnorm_prologue_rejects_what_it_cannot_fuse() -> None:
+    from heliostune_b200.action_configs import ActionCandidate, StreamConfig
+    from heliostune_b200.fusion import rmsnorm_matmul
+
+    x, gamma = _inputs(200, 4096, seed=3)
+    w = torch.zeros((4096, 1024), device="cuda", dtype=torch.float16)
+    with pytest.raises(ValueError, match="fused RMSNorm"):
+        rmsnorm_matmul(x, gamma, w, ActionCandidate(StreamConfig(256, 128, 64, 4, 4, 0)), fused=True)
+    # the unfused path still serves it
+    out = rmsnorm_matmul(x, gamma, w, ActionCandidate(StreamConfig(256, 128, 64, 4, 4, 0)))
+    assert out.shape == (200, 1024) and bool((out == 0).all())
