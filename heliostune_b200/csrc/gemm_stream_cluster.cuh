@@ -73,9 +73,12 @@ struct ClusterStreamShape {
   static constexpr int kBarrierBytes = 256 + 16 * kStreamMaxStages;
   static constexpr bool kAsyncPush = MP <= 64;  // see the file comment
   // Shared memory below the barriers: ring and exchange side by side, or overlaid.
+  // Shared memory below the barriers: ring and exchange side by side, or overlaid; then the
+  // per-stage gamma slices of the RMSNorm prologue.
   __host__ __device__ static constexpr int data_bytes(int stages, int splits, bool early) {
-    return early ? stages * kStageBytes + exchange_bytes(splits)
-                 : (stages * kStageBytes > exchange_bytes(splits) ? stages * kStageBytes : exchange_bytes(splits));
+    return (early ? stages * kStageBytes + exchange_bytes(splits)
+                  : (stages * kStageBytes > exchange_bytes(splits) ? stages * kStageBytes : exchange_bytes(splits))) +
+           stages * BK * 2;
   }
   static constexpr int smem_bytes(int stages, int splits, bool early) {
     return 1024 + data_bytes(stages, splits, early) + kBarrierBytes;
@@ -95,6 +98,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   uint8_t* ring = smem;
   uint8_t* exchange = early ? ring + stages * S::kStageBytes : ring;  // the S slots [MP][W]
   uint64_t* bars = reinterpret_cast<uint64_t*>(ring + S::data_bytes(stages, args.splits, early));
+  __half* gamma_ring = reinterpret_cast<__half*>(bars) - stages * BK;  // [stage][BK] (RMSNorm)
   uint64_t* full = bars;
   uint64_t* empty = bars + kStreamMaxStages;
   uint64_t* tmem_full = bars + 2 * kStreamMaxStages;
@@ -160,8 +164,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         break;
       }
       uint8_t* st = ring + stage * S::kStageBytes;
-      mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
       const int k0 = kb * BK;
+      const int gamma_bytes = args.norm ? min(BK, args.k - k0) * 2 : 0;  // K % 8 == 0: 16-byte multiple
+      mbar_arrive_expect_tx(&full[stage], S::kStageBytes + gamma_bytes);
+      if (gamma_bytes > 0)
+        bulk_load_global(gamma_ring + stage * BK, args.gamma + k0, static_cast<uint32_t>(gamma_bytes), &full[stage]);
 #pragma unroll
       for (int na = 0; na < S::kAtomsN; ++na) {
         tma_load_2d(st + na * S::kWBoxBytes, &map_b, &full[stage], n0 + 64 * na, k0, stream_policy);
@@ -237,18 +244,21 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           break;
         }
         const uint32_t x_base = smem_addr(ring + stage * S::kStageBytes + S::kWBytes);
+        const uint32_t g_base = smem_addr(gamma_ring + stage * BK);
         if (row < MP) {
-#pragma unroll 1
+#pragma unroll
           for (int ka = 0; ka < S::kAtomsK; ++ka) {
             const uint32_t row_addr = x_base + ka * S::kXBoxBytes + row * 128;
-            for (int p = t % kTpr; p < 8; p += kTpr) {
+#pragma unroll
+            for (int i = 0; i < 8 / kTpr; ++i) {
+              const int p = t % kTpr + i * kTpr;
               const uint32_t addr = row_addr + (static_cast<uint32_t>(p) << 4);
-              const int k = kb * BK + ka * 64 + ((p ^ (row & 7)) << 3);  // swizzled chunk position
+              const int kl = ka * 64 + ((p ^ (row & 7)) << 3);  // swizzled chunk: its K offset in the block
               float4 raw = ld_shared_f32x4(addr);
               __half* h = reinterpret_cast<__half*>(&raw);
-              uint4 g = make_uint4(0, 0, 0, 0);
-              if (k < args.k) g = *reinterpret_cast<const uint4*>(args.gamma + k);
-              const __half* gh = reinterpret_cast<const __half*>(&g);
+              float4 graw = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (kb * BK + kl < args.k) graw = ld_shared_f32x4(g_base + kl * 2);
+              const __half* gh = reinterpret_cast<const __half*>(&graw);
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
                 const float v = __half2float(h[e]);

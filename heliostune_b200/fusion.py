@@ -61,11 +61,14 @@ def rmsnorm_matmul(
 ) -> torch.Tensor:
     """``RMSNorm(x; gamma, eps) @ W`` -- the RMSNorm feeding the QKV projection.
 
-    Fused (weight-streaming candidates with ``block_m <= 128``, the default where it applies):
-    one launch of ``hst_rmsnorm_matmul_stream``, whose main loop rescales each x tile it loads by
-    gamma and sums the squares of its rows, and whose epilogue multiplies the FP32 results by
+    Fused (weight-streaming candidates with ``block_m <= 128``; the default for
+    ``block_m <= 32``, where it costs nothing over the GEMM alone): one launch of
+    ``hst_rmsnorm_matmul_stream``, whose main loop rescales each x tile it loads by gamma and sums
+    the squares of its rows, and whose epilogue multiplies the FP32 results by
     ``rsqrt(mean(x^2) + eps)`` -- no normalised copy of x, no second kernel. The products are
-    rounded once, after the row factor, instead of the reference's intermediate FP16 rows.
+    rounded once, after the row factor, instead of the reference's intermediate FP16 rows. From
+    64 rows on, rescaling the tiles in flight outlasts the stage it must hide behind, so the
+    unfused form is the default there.
 
     Unfused (any other candidate, or ``fused=False``): the normalised rows are produced exactly as
     the reference's formula rounds them, ``fp16((x * rsqrt(mean(x^2) + eps)) * gamma)``, by the
@@ -93,7 +96,7 @@ def rmsnorm_matmul(
         and x.device == w.device == gamma.device
     )
     if fused is None:
-        fused = can_fuse
+        fused = can_fuse and config.block_m <= 32
     elif fused and not can_fuse:
         raise ValueError("the fused RMSNorm GEMM needs a stream candidate with block_m <= 128 and aligned row-major operands")
     if not fused:
