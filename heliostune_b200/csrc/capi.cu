@@ -728,12 +728,13 @@ int launch_stream_cluster(const DeviceState& dev, const Operands& o, int stages,
   static std::atomic<uint64_t> smem_done{0};
   HST_TRY(allow_smem(stream_cluster_kernel<NA, MP, BK>, smem_done));
   // Exchange slots beside the ring when at least two stages still fit, else inside it.
+  const bool nrm = norm.gamma != nullptr;
   int early_stages = stages;
-  while (early_stages > 2 && S::smem_bytes(early_stages, splits, true) > kMaxDynamicSmem) --early_stages;
-  const bool early = S::kAsyncPush && splits > 1 && S::smem_bytes(early_stages, splits, true) <= kMaxDynamicSmem;
+  while (early_stages > 2 && S::smem_bytes(early_stages, splits, true, nrm) > kMaxDynamicSmem) --early_stages;
+  const bool early = S::kAsyncPush && splits > 1 && S::smem_bytes(early_stages, splits, true, nrm) <= kMaxDynamicSmem;
   if (early) stages = early_stages;
-  while (stages > 2 && S::smem_bytes(stages, splits, early) > kMaxDynamicSmem) --stages;
-  if (S::smem_bytes(stages, splits, early) > kMaxDynamicSmem)
+  while (stages > 2 && S::smem_bytes(stages, splits, early, nrm) > kMaxDynamicSmem) --stages;
+  if (S::smem_bytes(stages, splits, early, nrm) > kMaxDynamicSmem)
     return fail(HST_ERR_UNSUPPORTED, "stream tile does not fit shared memory");
   CUtensorMap ma_, mb_;
   HST_TRY(encode_tiled_2d(&ma_, o.a, o.k, o.m, o.lda, 64, MP));
@@ -756,7 +757,7 @@ int launch_stream_cluster(const DeviceState& dev, const Operands& o, int stages,
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(static_cast<unsigned>(cdiv(o.n, S::kNT)), static_cast<unsigned>(splits));
   lc.blockDim = dim3(kStreamThreads);
-  lc.dynamicSmemBytes = smem_for_tmem(S::smem_bytes(stages, splits, early), S::kTmemCols);
+  lc.dynamicSmemBytes = smem_for_tmem(S::smem_bytes(stages, splits, early, nrm), S::kTmemCols);
   lc.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;

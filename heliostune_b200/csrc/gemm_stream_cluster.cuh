@@ -63,9 +63,10 @@ struct ClusterStreamShape {
   __host__ __device__ static constexpr int owner_cols(int splits) {
     return ((kNT + splits - 1) / splits + 3) / 4 * 4;
   }
-  // The S exchange slots, [MP][owner_cols] FP32 each, then S row-sum slots of MP floats.
-  __host__ __device__ static constexpr int exchange_bytes(int splits) {
-    return splits * owner_cols(splits) * MP * 4 + splits * MP * 4;
+  // The S exchange slots, [MP][owner_cols] FP32 each, then (RMSNorm prologue) S row-sum slots
+  // of MP floats.
+  __host__ __device__ static constexpr int exchange_bytes(int splits, bool norm) {
+    return splits * owner_cols(splits) * MP * 4 + (norm ? splits * MP * 4 : 0);
   }
   static constexpr int kCols = NA * MP;
   static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128 : kCols <= 256 ? 256 : 512;
@@ -75,13 +76,14 @@ struct ClusterStreamShape {
   // Shared memory below the barriers: ring and exchange side by side, or overlaid.
   // Shared memory below the barriers: ring and exchange side by side, or overlaid; then the
   // per-stage gamma slices of the RMSNorm prologue.
-  __host__ __device__ static constexpr int data_bytes(int stages, int splits, bool early) {
-    return (early ? stages * kStageBytes + exchange_bytes(splits)
-                  : (stages * kStageBytes > exchange_bytes(splits) ? stages * kStageBytes : exchange_bytes(splits))) +
-           stages * BK * 2;
+  __host__ __device__ static constexpr int data_bytes(int stages, int splits, bool early, bool norm) {
+    return (early ? stages * kStageBytes + exchange_bytes(splits, norm)
+                  : (stages * kStageBytes > exchange_bytes(splits, norm) ? stages * kStageBytes
+                                                                         : exchange_bytes(splits, norm))) +
+           (norm ? stages * BK * 2 : 0);
   }
-  static constexpr int smem_bytes(int stages, int splits, bool early) {
-    return 1024 + data_bytes(stages, splits, early) + kBarrierBytes;
+  static constexpr int smem_bytes(int stages, int splits, bool early, bool norm) {
+    return 1024 + data_bytes(stages, splits, early, norm) + kBarrierBytes;
   }
 };
 
@@ -97,7 +99,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   const bool early = args.early != 0;
   uint8_t* ring = smem;
   uint8_t* exchange = early ? ring + stages * S::kStageBytes : ring;  // the S slots [MP][W]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + S::data_bytes(stages, args.splits, early));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + S::data_bytes(stages, args.splits, early, args.norm != 0));
   __half* gamma_ring = reinterpret_cast<__half*>(bars) - stages * BK;  // [stage][BK] (RMSNorm)
   uint64_t* full = bars;
   uint64_t* empty = bars + kStreamMaxStages;
@@ -254,19 +256,26 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
               const int p = t % kTpr + i * kTpr;
               const uint32_t addr = row_addr + (static_cast<uint32_t>(p) << 4);
               const int kl = ka * 64 + ((p ^ (row & 7)) << 3);  // swizzled chunk: its K offset in the block
-              float4 raw = ld_shared_f32x4(addr);
-              __half* h = reinterpret_cast<__half*>(&raw);
+              const float4 raw = ld_shared_f32x4(addr);
               float4 graw = make_float4(0.f, 0.f, 0.f, 0.f);
               if (kb * BK + kl < args.k) graw = ld_shared_f32x4(g_base + kl * 2);
-              const __half* gh = reinterpret_cast<const __half*>(&graw);
+              const uint32_t xw[4] = {__float_as_uint(raw.x), __float_as_uint(raw.y), __float_as_uint(raw.z),
+                                      __float_as_uint(raw.w)};
+              const uint32_t gw[4] = {__float_as_uint(graw.x), __float_as_uint(graw.y), __float_as_uint(graw.z),
+                                      __float_as_uint(graw.w)};
+              uint32_t out[4];
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const float v = __half2float(h[e]);
-                row_ss = fmaf(v, v, row_ss);
-                h[e] = __float2half_rn(v * __half2float(gh[e]));
+              for (int e = 0; e < 4; ++e) {
+                __half2 xh, gh;
+                memcpy(&xh, &xw[e], 4);
+                memcpy(&gh, &gw[e], 4);
+                const float2 v = __half22float2(xh);
+                const float2 g2 = __half22float2(gh);
+                row_ss = fmaf(v.x, v.x, row_ss);
+                row_ss = fmaf(v.y, v.y, row_ss);
+                out[e] = pack_half2(v.x * g2.x, v.y * g2.y);
               }
-              const uint32_t* w = reinterpret_cast<const uint32_t*>(&raw);
-              st_shared_v4(addr, w[0], w[1], w[2], w[3]);
+              st_shared_v4(addr, out[0], out[1], out[2], out[3]);
             }
           }
         }
@@ -355,12 +364,18 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         tmem_ld_wait();
         if (splits == 1) {
           if (n < args.n) {
+            if (!args.norm) {
 #pragma unroll
-            for (int j = 0; j < kChunk; ++j) {
-              const int m = c0 + j;
-              if (m < args.m) {
-                const float v = __uint_as_float(r[j]) * (args.norm ? row_factor(m) : 1.f);
-                args.c[static_cast<int64_t>(m) * args.ldc + n] = __float2half_rn(v);
+              for (int j = 0; j < kChunk; ++j) {
+                const int m = c0 + j;
+                if (m < args.m) args.c[static_cast<int64_t>(m) * args.ldc + n] = __float2half_rn(__uint_as_float(r[j]));
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < kChunk; ++j) {
+                const int m = c0 + j;
+                if (m < args.m)
+                  args.c[static_cast<int64_t>(m) * args.ldc + n] = __float2half_rn(__uint_as_float(r[j]) * row_factor(m));
               }
             }
           }
