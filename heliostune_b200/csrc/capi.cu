@@ -721,14 +721,14 @@ struct RowNorm {
   float eps = 0.f;
 };
 
-template <int NA, int MP, int BK>
+template <int NA, int MP, int BK, bool NORM>
 int launch_stream_cluster(const DeviceState& dev, const Operands& o, int stages, int splits,
                           int kb_per_split, cudaStream_t stream, const RowNorm& norm = RowNorm{}) {
   using S = ClusterStreamShape<NA, MP, BK>;
   static std::atomic<uint64_t> smem_done{0};
-  HST_TRY(allow_smem(stream_cluster_kernel<NA, MP, BK>, smem_done));
+  HST_TRY(allow_smem(stream_cluster_kernel<NA, MP, BK, NORM>, smem_done));
   // Exchange slots beside the ring when at least two stages still fit, else inside it.
-  const bool nrm = norm.gamma != nullptr;
+  constexpr bool nrm = NORM;
   int early_stages = stages;
   while (early_stages > 2 && S::smem_bytes(early_stages, splits, true, nrm) > kMaxDynamicSmem) --early_stages;
   const bool early = S::kAsyncPush && splits > 1 && S::smem_bytes(early_stages, splits, true, nrm) <= kMaxDynamicSmem;
@@ -748,7 +748,6 @@ int launch_stream_cluster(const DeviceState& dev, const Operands& o, int stages,
   args.splits = splits;
   args.stages = stages;
   args.early = early ? 1 : 0;
-  args.norm = norm.gamma != nullptr ? 1 : 0;
   args.eps = norm.eps;
   args.gamma = norm.gamma;
   args.status = dev.status;
@@ -766,16 +765,28 @@ int launch_stream_cluster(const DeviceState& dev, const Operands& o, int stages,
   attr[0].val.clusterDim.z = 1;
   lc.attrs = attr;
   lc.numAttrs = splits > 1 ? 1 : 0;
-  HST_CUDA(cudaLaunchKernelEx(&lc, stream_cluster_kernel<NA, MP, BK>, ma_, mb_, args));
+  HST_CUDA(cudaLaunchKernelEx(&lc, stream_cluster_kernel<NA, MP, BK, NORM>, ma_, mb_, args));
   return HST_OK;
+}
+
+// The plain kernel, or its RMSNorm-prologue instantiation when `norm` carries a gamma.
+template <int NA, int MP, int BK>
+int launch_stream_either(const DeviceState& dev, const Plan& p, const Operands& o,
+                         cudaStream_t stream, const RowNorm& norm) {
+  if (norm.gamma == nullptr)
+    return launch_stream_cluster<NA, MP, BK, false>(dev, o, p.stages, p.splits, p.kb_per_split, stream);
+  if constexpr (MP <= 128) {
+    return launch_stream_cluster<NA, MP, BK, true>(dev, o, p.stages, p.splits, p.kb_per_split, stream, norm);
+  } else {
+    return fail(HST_ERR_UNSUPPORTED, "the RMSNorm prologue covers up to 128 rows");
+  }
 }
 
 int dispatch_stream_cluster(const DeviceState& dev, const Plan& p, const Operands& o,
                             cudaStream_t stream, const RowNorm& norm = RowNorm{}) {
-#define HST_CLUSTER_CASE(NA_, MP_, BK_)                                                   \
-  if (p.nt == 128 * NA_ && p.mp == MP_ && p.bk == BK_)                                    \
-    return launch_stream_cluster<NA_, MP_, BK_>(dev, o, p.stages, p.splits, p.kb_per_split, \
-                                                stream, norm);
+#define HST_CLUSTER_CASE(NA_, MP_, BK_)                        \
+  if (p.nt == 128 * NA_ && p.mp == MP_ && p.bk == BK_)         \
+    return launch_stream_either<NA_, MP_, BK_>(dev, p, o, stream, norm);
   HST_CLUSTER_CASE(1, 16, 64)
   HST_CLUSTER_CASE(1, 32, 64)
   HST_CLUSTER_CASE(1, 64, 64)

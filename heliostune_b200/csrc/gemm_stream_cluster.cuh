@@ -20,7 +20,7 @@
 //     No workspace, no second kernel, no atomics; the result is bitwise reproducible.
 // With S = 1 the epilogue writes C straight from TMEM.
 //
-// RMSNorm prologue (args.norm): C = RMSNorm(A; gamma, eps) * B for an unnormalised A. While the
+// RMSNorm prologue (NORM = true): C = RMSNorm(A; gamma, eps) * B for an unnormalised A. While the
 // main loop runs, the four epilogue warps take every A^T tile as it lands, add its squares to
 // per-row FP32 sums and rewrite it in place as fp16(a * gamma[k]); the UMMAs wait for that
 // (a second barrier per stage). The row factors rsqrt(sum / K + eps) are applied to the FP32
@@ -38,9 +38,8 @@ struct ClusterStreamArgs {
   int splits;  // cluster size along y
   int stages;
   int early;   // exchange slots beside the ring (1) or in it after the main loops (0)
-  int norm;    // RMSNorm prologue on A (see the file comment)
-  float eps;
-  const __half* gamma;  // [k] when norm
+  float eps;            // RMSNorm prologue (NORM): eps and gamma [k]
+  const __half* gamma;
   int* status;
   __half* c;
   int64_t ldc;
@@ -87,7 +86,7 @@ struct ClusterStreamShape {
   }
 };
 
-template <int NA, int MP, int BK>
+template <int NA, int MP, int BK, bool NORM>
 __global__ void __launch_bounds__(kStreamThreads, 1)
     stream_cluster_kernel(const __grid_constant__ CUtensorMap map_a,
                           const __grid_constant__ CUtensorMap map_b, const ClusterStreamArgs args) {
@@ -99,7 +98,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   const bool early = args.early != 0;
   uint8_t* ring = smem;
   uint8_t* exchange = early ? ring + stages * S::kStageBytes : ring;  // the S slots [MP][W]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + S::data_bytes(stages, args.splits, early, args.norm != 0));
+  static_assert(!NORM || MP <= 128, "the RMSNorm prologue covers up to 128 rows");
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + S::data_bytes(stages, args.splits, early, NORM));
   __half* gamma_ring = reinterpret_cast<__half*>(bars) - stages * BK;  // [stage][BK] (RMSNorm)
   uint64_t* full = bars;
   uint64_t* empty = bars + kStreamMaxStages;
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     if (S::kAsyncPush && args.splits > 1) {
       const int w = S::owner_cols(args.splits);
       const int own_cols = min(w, S::kNT - split * w);
-      const int sums = args.norm ? args.m : 0;  // the row sums travel with the slices
+      const int sums = NORM ? args.m : 0;  // the row sums travel with the slices
       mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(args.splits * (args.m * own_cols + sums) * 4));
     }
     *abort_flag = 0;
@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       }
       uint8_t* st = ring + stage * S::kStageBytes;
       const int k0 = kb * BK;
-      const int gamma_bytes = args.norm ? min(BK, args.k - k0) * 2 : 0;  // K % 8 == 0: 16-byte multiple
+      const int gamma_bytes = NORM ? min(BK, args.k - k0) * 2 : 0;  // K % 8 == 0: 16-byte multiple
       mbar_arrive_expect_tx(&full[stage], S::kStageBytes + gamma_bytes);
       if (gamma_bytes > 0)
         bulk_load_global(gamma_ring + stage * BK, args.gamma + k0, static_cast<uint32_t>(gamma_bytes), &full[stage]);
@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     uint32_t phase = 0;
     bool ok = true;
     for (int kb = kb_begin; kb < kb_end; ++kb) {
-      if (!mbar_wait(args.norm ? &scaled[stage] : &full[stage], phase, abort_flag)) {
+      if (!mbar_wait(NORM ? &scaled[stage] : &full[stage], phase, abort_flag)) {
         raise_abort(args.status, abort_flag, kStatusMmaTimeout);
         ok = false;
         break;
@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     umma_commit(mma_done);
     if (!mbar_wait(mma_done, 0, nullptr, 200000000ull)) atomicOr(args.status, kStatusDrainTimeout);
   } else if (warp >= 2) {
-    if (args.norm) {
+    if constexpr (NORM) {
       // ---------------- RMSNorm prologue: sum of squares and gamma on every A^T tile ----------
       // Thread t owns row t / kTpr of the tile and every kTpr-th 16-byte chunk of that row.
       const int t = threadIdx.x - 64;
@@ -318,7 +318,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     }
     return rsqrtf(ss / static_cast<float>(args.k) + args.eps);
   };
-  if (warp >= 2 && args.norm) {
+  if (NORM && warp >= 2) {
     // ---- this CTA's row sums to every owner (with the slices), or to its own table ----
     const int t = threadIdx.x - 64;
     const int row = t / kTpr;
@@ -364,7 +364,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         tmem_ld_wait();
         if (splits == 1) {
           if (n < args.n) {
-            if (!args.norm) {
+            if constexpr (!NORM) {
 #pragma unroll
               for (int j = 0; j < kChunk; ++j) {
                 const int m = c0 + j;
@@ -421,7 +421,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         acc.z += v.z;
         acc.w += v.w;
       }
-      if (args.norm) {
+      if constexpr (NORM) {
         const float f = row_factor(m);
         acc.x *= f;
         acc.y *= f;
