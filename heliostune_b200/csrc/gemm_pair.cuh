@@ -404,9 +404,9 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       __syncwarp();
       if (lane == 0) {
         if (rank == 0) {
-          mbar_arrive(&tmem_empty[which]);
+          mbar_arrive_relaxed(&tmem_empty[which]);
         } else {
-          mbar_arrive_cluster(map_to_rank(smem_addr(&tmem_empty[which]), leader));
+          mbar_arrive_cluster_relaxed(map_to_rank(smem_addr(&tmem_empty[which]), leader));
         }
       }
     };
@@ -462,37 +462,9 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           have = __all_sync(0xffffffffu, have);
           if (!have && lane == 0) raise_abort(args.status, abort_flag, kStatusEpilogueTimeout);
         }
-#pragma unroll 1
-        for (int c = 0; c < BN / 64 && have; ++c) {
-          const uint32_t taddr = lane_tmem + c * 64;
-          uint32_t lo[32], hi[32];
-          tmem_ld_32x32b_x32(taddr, lo);
-          tmem_ld_32x32b_x32(taddr + 32, hi);
-          tmem_ld_wait();
-          if (!released0 && c * 64 + 64 == 256) {
-            release_acc(0);
-            released0 = true;
-          }
-          if (finisher) {
-            // Add the later K ranges in K order (pair - 1 first).
-            int64_t pos = work.it;
-            for (int q = pair - 1; q >= 0 && pos < tile_end; --q) {
-              const int64_t end = PairWork::share_end(work.total, pairs, q);
-              if (end > pos) {
-                const float* part = slot_of_pair(q) + (static_cast<size_t>(c * 16) * 128 + row) * 4;
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  const float4 p = ld_global_cg_f32x4(part + static_cast<size_t>(j) * 128 * 4);
-                  uint32_t* d = j < 8 ? &lo[4 * j] : &hi[4 * (j - 8)];
-                  d[0] = __float_as_uint(__uint_as_float(d[0]) + p.x);
-                  d[1] = __float_as_uint(__uint_as_float(d[1]) + p.y);
-                  d[2] = __float_as_uint(__uint_as_float(d[2]) + p.z);
-                  d[3] = __float_as_uint(__uint_as_float(d[3]) + p.w);
-                }
-                pos = end;
-              }
-            }
-          }
+        // Sub-tile c (64 columns) through staging buffer `buf`: one TMA store, and the peers'
+        // copies when the tile fans out.
+        auto drain = [&](int c, const uint32_t (&lo)[32], const uint32_t (&hi)[32]) {
           uint8_t* dst = staging + buf * kEpilogueStageBytes;
           if (lane == 0) bulk_wait_group_read<1>();
           __syncwarp();
@@ -535,6 +507,63 @@ __global__ void __launch_bounds__(kTileThreads, 1)
             }
           }
           buf ^= 1;
+        };
+        if (!finisher) {
+          // A whole tile: sub-tile c + 1's TMEM loads are in flight while sub-tile c is stored.
+          uint32_t lo[2][32], hi[2][32];
+          tmem_ld_32x32b_x32(lane_tmem, lo[0]);
+          tmem_ld_32x32b_x32(lane_tmem + 32, hi[0]);
+          tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < BN / 64; ++c) {
+            const int cur = c & 1;
+            if (c + 1 < BN / 64) {
+              tmem_ld_32x32b_x32(lane_tmem + (c + 1) * 64, lo[cur ^ 1]);
+              tmem_ld_32x32b_x32(lane_tmem + (c + 1) * 64 + 32, hi[cur ^ 1]);
+            }
+            drain(c, lo[cur], hi[cur]);
+            if (c + 1 < BN / 64) {
+              tmem_ld_wait();
+              tmem_ld_fence_regs(lo[cur ^ 1]);
+              tmem_ld_fence_regs(hi[cur ^ 1]);
+              if (!released0 && (c + 2) * 64 == 256) {
+                release_acc(0);
+                released0 = true;
+              }
+            }
+          }
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < BN / 64 && have; ++c) {
+            const uint32_t taddr = lane_tmem + c * 64;
+            uint32_t lo[32], hi[32];
+            tmem_ld_32x32b_x32(taddr, lo);
+            tmem_ld_32x32b_x32(taddr + 32, hi);
+            tmem_ld_wait();
+            if (!released0 && c * 64 + 64 == 256) {
+              release_acc(0);
+              released0 = true;
+            }
+            // Add the later K ranges in K order (pair - 1 first).
+            int64_t pos = work.it;
+            for (int q = pair - 1; q >= 0 && pos < tile_end; --q) {
+              const int64_t end = PairWork::share_end(work.total, pairs, q);
+              if (end > pos) {
+                const float* part = slot_of_pair(q) + (static_cast<size_t>(c * 16) * 128 + row) * 4;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const float4 p = ld_global_cg_f32x4(part + static_cast<size_t>(j) * 128 * 4);
+                  uint32_t* d = j < 8 ? &lo[4 * j] : &hi[4 * (j - 8)];
+                  d[0] = __float_as_uint(__uint_as_float(d[0]) + p.x);
+                  d[1] = __float_as_uint(__uint_as_float(d[1]) + p.y);
+                  d[2] = __float_as_uint(__uint_as_float(d[2]) + p.z);
+                  d[3] = __float_as_uint(__uint_as_float(d[3]) + p.w);
+                }
+                pos = end;
+              }
+            }
+            drain(c, lo, hi);
+          }
         }
       }
       if (!released0) release_acc(0);

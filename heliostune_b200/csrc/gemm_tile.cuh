@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       }
       tc_fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+      if (lane == 0) mbar_arrive_relaxed(&tmem_empty[acc]);
       if (++acc == S::kAccBufs) {
         acc = 0;
         acc_phase ^= 1u;

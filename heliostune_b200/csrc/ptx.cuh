@@ -55,6 +55,15 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// Arrive without release semantics, for a barrier that orders execution only: a TMEM
+// accumulator reported drained after tcgen05.wait::ld, whose data is already in registers. A
+// release arrive would also wait for this thread's earlier stores (bulk tensor stores included),
+// which the waiting thread never reads.
+__device__ __forceinline__ void mbar_arrive_relaxed(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
                "r"(bytes)
@@ -251,6 +260,14 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Marks registers filled by a tcgen05.ld as redefined here, so that no use of them is moved
+// above the tcgen05.wait::ld that precedes this call (needed while other loads stay in flight).
+template <int N>
+__device__ __forceinline__ void tmem_ld_fence_regs(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
 // ------------------------------------------------------------------------------------------
 // CTA pairs (clusters of two CTAs sharing one cta_group::2 UMMA)
 // ------------------------------------------------------------------------------------------
@@ -443,6 +460,12 @@ __device__ __forceinline__ void cluster_sync() {
 // Arrive on an mbarrier that may live in the peer CTA (shared::cluster address).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+// The relaxed form of mbar_arrive_cluster (see mbar_arrive_relaxed).
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
 }
 
