@@ -287,14 +287,18 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     int tile, kb0, kb1;
     // UMMAs of one K block of stage `st` into accumulator columns [col, col + kUmmaN); B atoms
     // from `b_atom` on. `first`: the segment's first K block (overwrite instead of accumulate).
+    // Stage 0's A and B descriptors at K step 0. Any other operand's descriptor adds its byte
+    // offset / 16 to the start-address field (bits 0-13; shared memory stays below 256 KB).
+    const uint64_t a_desc0 = smem_desc(smem_addr(ring), 16, 1024);
+    const uint64_t b_desc0 = smem_desc(smem_addr(ring) + S::kABytes, S::kBBoxBytes, 1024);
     auto issue = [&](int st, uint32_t col, int b_atom, bool first) {
-      const uint32_t a_base = smem_addr(ring + st * S::kStageBytes);
-      const uint32_t b_base = a_base + S::kABytes + b_atom * S::kBBoxBytes;
+      const uint64_t a_st = a_desc0 + static_cast<uint64_t>(st * (S::kStageBytes >> 4));
+      const uint64_t b_st = b_desc0 + static_cast<uint64_t>(st * (S::kStageBytes >> 4) +
+                                                            b_atom * (S::kBBoxBytes >> 4));
 #pragma unroll
       for (int kk = 0; kk < BK / 16; ++kk) {
-        const uint64_t adesc =
-            smem_desc(a_base + (kk >> 2) * S::kABoxBytes + (kk & 3) * 32, 16, 1024);
-        const uint64_t bdesc = smem_desc(b_base + kk * 2048, S::kBBoxBytes, 1024);
+        const uint64_t adesc = a_st + (((kk >> 2) * S::kABoxBytes + (kk & 3) * 32) >> 4);
+        const uint64_t bdesc = b_st + ((kk * 2048) >> 4);
         umma_f16_pair(tmem_base + col, adesc, bdesc, S::kIdesc, (!first || kk != 0) ? 1u : 0u);
       }
     };

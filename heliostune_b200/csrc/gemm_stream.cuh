@@ -143,6 +143,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------- UMMA issuer ----------------
+    // Stage 0's operand descriptors at K step 0; any other operand adds its byte offset / 16 to
+    // the start-address field (bits 0-13; shared memory stays below 256 KB).
+    const uint64_t w_desc0 = smem_desc(smem_addr(ring), S::kWBoxBytes, 1024);
+    const uint64_t x_desc0 = smem_desc(smem_addr(ring) + S::kWBytes, 16, 1024);
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -153,13 +157,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         break;
       }
       tc_fence_after_sync();
-      const uint32_t w_base = smem_addr(ring + stage * S::kStageBytes);
-      const uint32_t x_base = w_base + S::kWBytes;
+      const uint64_t stage_off = static_cast<uint64_t>(stage * (S::kStageBytes >> 4));
 #pragma unroll
       for (int kk = 0; kk < BK / 16; ++kk) {
-        const uint64_t adesc = smem_desc(w_base + kk * 2048, S::kWBoxBytes, 1024);
+        const uint64_t adesc = w_desc0 + stage_off + ((kk * 2048) >> 4);
         const uint64_t bdesc =
-            smem_desc(x_base + (kk >> 2) * S::kXBoxBytes + (kk & 3) * 32, 16, 1024);
+            x_desc0 + stage_off + (((kk >> 2) * S::kXBoxBytes + (kk & 3) * 32) >> 4);
         umma_f16(tmem_base, adesc, bdesc, S::kIdesc, (kb != kb_begin || kk != 0) ? 1u : 0u);
       }
       umma_commit(&empty[stage]);

@@ -165,6 +165,10 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------- UMMA issuer ----------------
+    // Stage 0's operand descriptors at K step 0; any other operand adds its byte offset / 16 to
+    // the start-address field (bits 0-13; shared memory stays below 256 KB).
+    const uint64_t a_desc0 = smem_desc(smem_addr(ring), 16, 1024);
+    const uint64_t b_desc0 = smem_desc(smem_addr(ring) + S::kABytes, S::kBBoxBytes, 1024);
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
@@ -185,17 +189,16 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           break;
         }
         tc_fence_after_sync();
-        const uint32_t a_base = smem_addr(ring + stage * S::kStageBytes);
-        const uint32_t b_base = a_base + S::kABytes;
+        const uint64_t stage_off = static_cast<uint64_t>(stage * (S::kStageBytes >> 4));
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
           const int ka = kk >> 2;
           const int kin = kk & 3;
-          const uint64_t bdesc = smem_desc(b_base + kk * 2048, S::kBBoxBytes, 1024);
+          const uint64_t bdesc = b_desc0 + stage_off + ((kk * 2048) >> 4);
 #pragma unroll
           for (int ma = 0; ma < MA; ++ma) {
-            const uint64_t adesc = smem_desc(
-                a_base + (ma * S::kAtomsK + ka) * S::kABoxBytes + kin * 32, 16, 1024);
+            const uint64_t adesc =
+                a_desc0 + stage_off + (((ma * S::kAtomsK + ka) * S::kABoxBytes + kin * 32) >> 4);
             umma_f16(d_base + ma * BN, adesc, bdesc, S::kIdesc, (kb | kk) != 0);
           }
         }
