@@ -318,10 +318,35 @@ def pair_stream_k_tiles(tiles: int, k_blocks: int, pairs: int) -> int:
 
 
 #: 512-wide pair tiles (a quarter fewer L2-to-SM bytes per FLOP, single-buffered accumulator),
-#: offered once the 256 x 512 tiles fill a wave of pairs; the stream-K form where they leave the
-#: last wave part-filled.
+#: offered while the 256 x 512 tiles keep at least :data:`PAIR_MIN_FILL` of the pairs busy over
+#: their waves; the stream-K form where they leave the last wave part-filled.
 PAIR_WIDE = ActionCandidate(PairConfig(256, 512, 64, 4, 4, 16))
 PAIR_WIDE_STREAM_K = ActionCandidate(PairConfig(256, 512, 64, 4, 4, 8, PAIR_STREAM_K))
+#: Busy fraction of the pairs (:func:`wave_fill`) under which a tile shape counts as underfilling.
+PAIR_MIN_FILL = 0.75
+#: 128-deep K blocks on the 256 x 256 tile: half the ring waits per multiply-add (three stages).
+PAIR_DEEP_K = ActionCandidate(PairConfig(256, 256, 128, 4, 3, 8))
+#: 256 x 128 tiles with 128-deep K blocks, twice as many tiles as 256 x 256: offered (with the
+#: frozen 128 x 128 tile) while the 256 x 256 tiles underfill the pairs and M is at most
+#: :data:`PAIR_NARROW_M_MAXIMUM`.
+PAIR_NARROW = ActionCandidate(PairConfig(256, 128, 128, 4, 4, 8))
+PAIR_NARROW_M_MAXIMUM = 1024
+
+
+def wave_fill(tiles: int, slots: int) -> float:
+    """Busy fraction of ``slots`` persistent workers over the waves ``tiles`` equal tiles take."""
+    if tiles <= 0 or slots <= 0:
+        return 0.0
+    return tiles / (slots * -(-tiles // slots))
+
+
+def pair_tiles_underfill(workload: Workload, sm_count: int = 148) -> bool:
+    """Whether narrower tiles than 256 x 256 are worth offering (see :data:`PAIR_NARROW`)."""
+    tiles = -(-workload.m // 256) * -(-workload.n // 256)
+    return (
+        workload.m <= PAIR_NARROW_M_MAXIMUM
+        and wave_fill(tiles, resident_clusters(2, sm_count)) < PAIR_MIN_FILL
+    )
 
 
 def pair_candidates_for(workload: Workload, sm_count: int = 148) -> tuple[ActionCandidate, ...]:
@@ -332,17 +357,19 @@ def pair_candidates_for(workload: Workload, sm_count: int = 148) -> tuple[Action
     wide_tiles = -(-workload.m // 256) * -(-workload.n // 512)
     k_blocks = -(-workload.k // 64)
     pairs = resident_clusters(2, sm_count)
-    extra = ()
+    extra = (PAIR_DEEP_K,)
     if tiles <= 33:
         extra += (PAIR_SPLIT2,)
     if tiles <= 15:
         extra += (PAIR_SPLIT4,)
     if pair_stream_k_tiles(tiles, k_blocks, pairs) > 0:
         extra += (PAIR_STREAM_K_CANDIDATE,)
-    if wide_tiles >= pairs:
+    if wave_fill(wide_tiles, pairs) >= PAIR_MIN_FILL:
         extra += (PAIR_WIDE,)
         if pair_stream_k_tiles(wide_tiles, k_blocks, pairs) > 0:
             extra += (PAIR_WIDE_STREAM_K,)
+    if pair_tiles_underfill(workload, sm_count):
+        extra += (PAIR_NARROW,)
     return _sorted((*PAIR_CANDIDATES, *extra))
 
 
@@ -360,12 +387,20 @@ B200_FROZEN_KEPT = frozenset(
 )
 
 
+#: The frozen tile that still wins a grid shape beside the CTA-pair family (M = 512), offered
+#: where :func:`pair_tiles_underfill`; elsewhere above M = 128 the pair family alone is offered.
+B200_FROZEN_KEPT_WITH_PAIRS = frozenset({"tile:m128n128k128-w8s3g8"})
+
+
 def b200_candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:
     """Everything the B200 tuner may probe: the frozen candidates of :data:`B200_FROZEN_KEPT`
     that apply to the workload, plus the B200 families."""
     frozen = tuple(c for c in candidates_for(workload) if c.key in B200_FROZEN_KEPT)
     if workload.m <= 31:
         frozen = tuple(c for c in frozen if c.family == "split_k")
+    elif workload.m >= PAIR_M_MINIMUM:
+        keep = B200_FROZEN_KEPT_WITH_PAIRS if pair_tiles_underfill(workload) else frozenset()
+        frozen = tuple(c for c in frozen if c.key in keep)
     return _sorted((*frozen, *stream_candidates_for(workload), *pair_candidates_for(workload)))
 
 

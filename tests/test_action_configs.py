@@ -13,6 +13,8 @@ from heliostune_b200.action_configs import (
     ALL_CANDIDATES,
     B200_FROZEN_KEPT,
     NON_SPLIT_CANDIDATES,
+    PAIR_DEEP_K,
+    PAIR_NARROW,
     SPLIT_K_CANDIDATES,
     ActionCandidate,
     SplitKConfig,
@@ -23,10 +25,12 @@ from heliostune_b200.action_configs import (
     PairConfig,
     pair_candidates_for,
     pair_stream_k_tiles,
+    pair_tiles_underfill,
     split_plan,
     stream_block_m,
     stream_candidates_for,
     stream_splits,
+    wave_fill,
 )
 from heliostune_b200.configs import (
     DEFAULT_CONFIGS,
@@ -260,14 +264,37 @@ def test_pair_stream_k_rule() -> None:
     assert "pair:pair-m256n256k64-w4s6g8-streamk" not in {c.key for c in pair_candidates_for(replace(w, m=8192, n=9472))}
 
 
-def test_wide_pair_candidates_need_a_full_wave() -> None:
+def test_wide_pair_candidates_need_well_filled_waves() -> None:
     def keys(m: int, n: int, k: int) -> set[str]:
         return {c.key for c in pair_candidates_for(Workload(m, n, k, "x", "y", "z"))}
 
+    assert wave_fill(72, 74) == 72 / 74 and wave_fill(96, 74) == 96 / 148 and wave_fill(0, 74) == 0.0
     assert "pair:pair-m256n512k64-w4s4g16" not in keys(512, 4096, 4096)  # 16 wide tiles
+    assert "pair:pair-m256n512k64-w4s4g16" in keys(2048, 4096, 4096)  # 64 of 74 pairs busy
+    assert "pair:pair-m256n512k64-w4s4g16" not in keys(2048, 6144, 4096)  # 96 = 74 + 22
     assert "pair:pair-m256n512k64-w4s4g16" in keys(8192, 4096, 4096)  # 256 wide tiles
     assert "pair:pair-m256n512k64-w4s4g8-streamk" in keys(8192, 4096, 14336)  # 256 = 3 x 74 + 34
     assert "pair:pair-m256n512k64-w4s4g8-streamk" not in keys(8192, 37888, 3584)  # 32 x 74 exactly
+
+
+def test_deep_k_and_narrow_pair_candidates() -> None:
+    def pool(m: int, n: int, k: int) -> set[str]:
+        return {c.key for c in b200_candidates_for(Workload(m, n, k, "x", "y", "z"))}
+
+    for shape in ((512, 4608, 3584), (2048, 6144, 4096), (8192, 37888, 3584)):
+        assert PAIR_DEEP_K.key in pool(*shape)
+        assert "tile:m128n256k64-w8s4g8" not in pool(*shape)
+    # 256 x 256 tiles: 36 for M = 512, N = 4608 (half the pairs idle); 224 for N = 28672.
+    assert pair_tiles_underfill(Workload(512, 4608, 3584, "x", "y", "z"))
+    assert {PAIR_NARROW.key, "tile:m128n128k128-w8s3g8"} <= pool(512, 4608, 3584)
+    assert not pair_tiles_underfill(Workload(512, 28672, 4096, "x", "y", "z"))
+    assert not {PAIR_NARROW.key, "tile:m128n128k128-w8s3g8"} & pool(512, 28672, 4096)
+    assert not pair_tiles_underfill(Workload(2048, 1024, 4096, "x", "y", "z"))  # M above 1024
+    assert "tile:m128n256k64-w8s4g8" in pool(128, 28672, 4096)
+    for m, n, k in ((512, 3584, 3584), (512, 28672, 4096), (2048, 4608, 3584), (8192, 4096, 14336)):
+        assert len(pool(m, n, k)) <= 8  # every candidate gets one of the bandit's probes
+
+
     with pytest.raises(SchemaError):
         PairConfig(256, 512, 128, 4, 4, 8)
     with pytest.raises(SchemaError):

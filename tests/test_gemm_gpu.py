@@ -17,6 +17,8 @@ from heliostune_b200 import _native
 from heliostune_b200.action_configs import (
     ALL_CANDIDATES,
     PAIR_CANDIDATES,
+    PAIR_DEEP_K,
+    PAIR_NARROW,
     PAIR_STREAM_K,
     PairConfig,
     NON_SPLIT_CANDIDATES,
@@ -123,7 +125,7 @@ def test_stream_odd_cluster_sizes(split: int, block_n: int, shape: tuple[int, in
     assert torch.equal(first.view(torch.int16), launch(a, b, candidate).view(torch.int16))
 
 
-@pytest.mark.parametrize("candidate", PAIR_CANDIDATES, ids=lambda c: c.key)
+@pytest.mark.parametrize("candidate", (*PAIR_CANDIDATES, PAIR_DEEP_K, PAIR_NARROW), ids=lambda c: c.key)
 @pytest.mark.parametrize(
     "shape",
     ((512, 4096, 4096), (257, 264, 136), (1000, 1032, 520), (131, 8, 8), (2048, 3584, 18944)),
@@ -353,6 +355,8 @@ def test_full_size_grid_shapes(workload: Workload) -> None:
         ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8)),
         ActionCandidate(PairConfig(256, 256, 64, 4, 6, 8, PAIR_STREAM_K)),
         ActionCandidate(PairConfig(256, 512, 64, 4, 4, 16)),
+        PAIR_DEEP_K,
+        PAIR_NARROW,
     ],
     ids=lambda c: c.key,
 )
