@@ -117,6 +117,29 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   const int kb_begin = split * args.kb_per_split;
   const int kb_end = min(kb_begin + args.kb_per_split, args.k_blocks);
 
+  // One stage's loads, completing on full[stage]: the W atoms, the X atoms and, with the RMSNorm
+  // prologue, the stage's slice of gamma.
+  auto load_stage = [&](int kb, int stage, uint64_t stream_policy, uint64_t keep_policy) {
+    uint8_t* st = ring + stage * S::kStageBytes;
+    const int k0 = kb * BK;
+    const int gamma_bytes = NORM ? min(BK, args.k - k0) * 2 : 0;  // K % 8 == 0: 16-byte multiple
+    mbar_arrive_expect_tx(&full[stage], S::kStageBytes + gamma_bytes);
+    if (gamma_bytes > 0)
+      bulk_load_global(gamma_ring + stage * BK, args.gamma + k0, static_cast<uint32_t>(gamma_bytes), &full[stage]);
+#pragma unroll
+    for (int na = 0; na < S::kAtomsN; ++na) {
+      tma_load_2d(st + na * S::kWBoxBytes, &map_b, &full[stage], n0 + 64 * na, k0, stream_policy);
+    }
+#pragma unroll
+    for (int ka = 0; ka < S::kAtomsK; ++ka) {
+      tma_load_2d(st + S::kWBytes + ka * S::kXBoxBytes, &map_a, &full[stage], k0 + 64 * ka, 0,
+                  keep_policy);
+    }
+  };
+  // Stages thread 0 (the producer) loaded before the CTA barrier: the first pass over the ring
+  // needs no free stage, so its loads overlap TMEM allocation and the barrier.
+  int preloaded = 0;
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
@@ -136,6 +159,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     fence_mbarrier_init();
     tma_prefetch_map(&map_a);
     tma_prefetch_map(&map_b);
+    preloaded = max(0, min(stages, kb_end - kb_begin));
+    const uint64_t stream_policy = l2_policy_evict_first();
+    const uint64_t keep_policy = l2_policy_evict_last();
+    for (int s = 0; s < preloaded; ++s) load_stage(kb_begin + s, s, stream_policy, keep_policy);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, S::kTmemCols);
@@ -155,31 +182,17 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     // ---------------- TMA producer ----------------
     const uint64_t stream_policy = l2_policy_evict_first();
     const uint64_t keep_policy = l2_policy_evict_last();
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t issued_mask = 0, issued_parity = 0;
+    int stage = preloaded == stages ? 0 : preloaded;
+    uint32_t phase = preloaded == stages ? 1u : 0u;
+    uint32_t issued_mask = (1u << preloaded) - 1u, issued_parity = 0;
     bool ok = true;
-    for (int kb = kb_begin; kb < kb_end; ++kb) {
+    for (int kb = kb_begin + preloaded; kb < kb_end; ++kb) {
       if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
         raise_abort(args.status, abort_flag, kStatusProducerTimeout);
         ok = false;
         break;
       }
-      uint8_t* st = ring + stage * S::kStageBytes;
-      const int k0 = kb * BK;
-      const int gamma_bytes = NORM ? min(BK, args.k - k0) * 2 : 0;  // K % 8 == 0: 16-byte multiple
-      mbar_arrive_expect_tx(&full[stage], S::kStageBytes + gamma_bytes);
-      if (gamma_bytes > 0)
-        bulk_load_global(gamma_ring + stage * BK, args.gamma + k0, static_cast<uint32_t>(gamma_bytes), &full[stage]);
-#pragma unroll
-      for (int na = 0; na < S::kAtomsN; ++na) {
-        tma_load_2d(st + na * S::kWBoxBytes, &map_b, &full[stage], n0 + 64 * na, k0, stream_policy);
-      }
-#pragma unroll
-      for (int ka = 0; ka < S::kAtomsK; ++ka) {
-        tma_load_2d(st + S::kWBytes + ka * S::kXBoxBytes, &map_a, &full[stage], k0 + 64 * ka, 0,
-                    keep_policy);
-      }
+      load_stage(kb, stage, stream_policy, keep_policy);
       issued_mask |= 1u << stage;
       issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
       if (++stage == stages) {
@@ -412,9 +425,20 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     const int quads = own_cols / 4;
     const int items = args.m * quads;
     const bool vec_store = (args.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(args.c) & 7) == 0);
-    for (int i = threadIdx.x; arrived && i < items; i += blockDim.x) {
-      const int m = i / quads;
-      const int q = i % quads;
+    // Item i is row i / quads, quad i % quads; a thread takes items t, t + T, t + 2T, ... (T
+    // threads), two at a time so both items' shared loads are in flight together.
+    const int step = static_cast<int>(blockDim.x);
+    const int dm = step / quads, dq = step % quads;
+    int m1 = static_cast<int>(threadIdx.x) / quads, q1 = static_cast<int>(threadIdx.x) % quads;
+    auto advance = [&](int& m, int& q) {
+      m += dm;
+      q += dq;
+      if (q >= quads) {
+        q -= quads;
+        ++m;
+      }
+    };
+    auto reduce = [&](int m, int q) {
       const uint32_t offset = static_cast<uint32_t>((m * cols + q * 4) * 4);
       float4 acc = ld_shared_f32x4(base + offset);
       for (int s = 1; s < splits; ++s) {
@@ -424,6 +448,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         acc.z += v.z;
         acc.w += v.w;
       }
+      return acc;
+    };
+    auto store = [&](int m, int q, float4 acc) {
       if constexpr (NORM) {
         const float f = row_factor(m);
         acc.x *= f;
@@ -444,6 +471,18 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
         for (int j = 0; j < 4 && n + j < args.n; ++j) dst[j] = __float2half_rn(vals[j]);
       }
+    };
+    for (int i = static_cast<int>(threadIdx.x); arrived && i < items; i += 2 * step) {
+      int m2 = m1, q2 = q1;
+      advance(m2, q2);
+      const bool second = i + step < items;
+      const float4 acc1 = reduce(m1, q1);
+      const float4 acc2 = second ? reduce(m2, q2) : acc1;
+      store(m1, q1, acc1);
+      if (second) store(m2, q2, acc2);
+      m1 = m2;
+      q1 = q2;
+      advance(m1, q1);
     }
   }
   (void)have_result;
