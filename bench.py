@@ -249,10 +249,6 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
             if w.key not in tuning.recommendations:
                 raise RuntimeError(f"no valid candidate for {w.key}")
             chosen[w.key] = tuning.recommendations[w.key]
-    tuning_s = time.perf_counter() - t0
-    del tune_operands
-    torch.cuda.empty_cache()
-
     # ---- 2. scored passes (bank 2) ---------------------------------------------------------
     def one_pass(fn_for, events) -> None:
         for i, w in enumerate(workloads):
@@ -297,6 +293,43 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
             dist.barrier()
         per_shape = [[events[s][i][0].elapsed_time(events[s][i][1]) for s in range(steps)] for i in range(n)]
         return per_shape, wall, (sampler.summary(epoch0, epoch1) if sampler else None)
+
+    # ---- 1b. confirmation (bank 1): the probes ran one candidate in a loop; the best ones are
+    # re-timed side by side, each after an L2 flush, in passes over all shapes (a different
+    # shape before every group), so clock drift over the passes hits every finalist alike ------
+    confirmed = 0
+    if args.confirm > 1 and not (args.force or args.choices):
+        finalists = {w.key: _finalists(tuning.probes[w.key], args.confirm, args.confirm_within) for w in workloads}
+        samples = {w.key: [[] for _ in finalists[w.key]] for w in workloads}
+        if world > 1:
+            dist.barrier()
+        for rnd in range(6):  # the first pass warms up
+            events = []
+            for w in workloads:
+                a, b = tune_operands[w.key]
+                count = len(finalists[w.key])
+                for j in range(count):
+                    f = (j + rnd) % count  # rotate the order from pass to pass
+                    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    flush.zero_()
+                    start.record()
+                    launch(a, b, finalists[w.key][f])
+                    end.record()
+                    events.append((w.key, f, start, end))
+            torch.cuda.synchronize()
+            if rnd > 0:
+                for key, f, start, end in events:
+                    samples[key][f].append(start.elapsed_time(end))
+        if world > 1:
+            dist.barrier()
+        for w in workloads:
+            medians = [statistics.median(t) for t in samples[w.key]]
+            best = finalists[w.key][medians.index(min(medians))]
+            confirmed += best.key != chosen[w.key].key
+            chosen[w.key] = best
+    tuning_s = time.perf_counter() - t0
+    del tune_operands
+    torch.cuda.empty_cache()
 
     ours_times, ours_wall, clocks = timed(ours_fn, args.steps, args.warmup, sample_clocks=True)
     cublas_times, _, _ = timed(cublas_fn, args.steps, args.warmup) if not args.skip_cublas else (ours_times, 0.0, None)
@@ -393,7 +426,16 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
             "workload": f"{args.workload}: {len(workloads)} shapes" if not args.shapes else f"shapes {args.shapes}",
             "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
             "l2": "256 MiB write before every launch",
-            "selection": f"Thompson bandit, {args.budget} probes per shape on bank-1 tensors; scored on bank-2 tensors",
+            "selection": (
+                f"Thompson bandit, {args.budget} probes per shape on bank-1 tensors"
+                + (
+                    f"; the best {args.confirm} probes within {args.confirm_within:.2f}x re-timed side by side in"
+                    f" 5 passes on bank-1 tensors ({confirmed} shapes changed)"
+                    if args.confirm > 1 and not (args.force or args.choices)
+                    else ""
+                )
+                + "; scored on bank-2 tensors"
+            ),
             "timing": "per-launch CUDA events on the launching stream; per-shape median over steps",
         },
         "geomean_latency_vs_cublas": round(geomean, 4),
@@ -668,6 +710,16 @@ def _traffic_from_profiles(family: str) -> dict[str, object]:
     }
 
 
+def _finalists(probes, count: int, within: float):
+    """Up to ``count`` probed candidates, fastest first, whose latency is within ``within`` x the
+    fastest probe's (the fastest alone if nothing else qualifies)."""
+    valid = sorted((p for p in probes if p.latency_ms is not None), key=lambda p: p.latency_ms)
+    if not valid:
+        raise RuntimeError("no valid probe")
+    best = valid[0].latency_ms
+    return [p.candidate for p in valid if p.latency_ms <= best * within][:count]
+
+
 def _e2e_pass(workloads, operands, chosen, device, steps: int):
     """Milliseconds of one pass over the workloads through the public API with host buffers.
 
@@ -805,6 +857,10 @@ def main() -> None:
     parser.add_argument("--shapes", default=None, help="comma list of MxNxK overriding the workload")
     parser.add_argument("--budget", type=int, default=8, help="bandit probes per shape")
     parser.add_argument("--probe-ms", type=float, default=10.0)
+    parser.add_argument(
+        "--confirm", type=int, default=3, help="re-time the best N probed candidates per shape in scored-like passes (1 = off)"
+    )
+    parser.add_argument("--confirm-within", type=float, default=1.10, help="finalists: probe latency within this factor of the best")
     parser.add_argument("--seed", type=int, default=0)
     parser.add_argument("--e2e-steps", type=int, default=1)
     parser.add_argument("--cpu-rows", type=int, default=64)
