@@ -41,6 +41,14 @@ if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 
 METRIC = "geomean latency/cuBLAS torch.matmul, 96-shape FP16 grid; TFLOP/s & % roofline"
+
+
+def _metric(args, count: int) -> str:
+    """BASELINE's metric name for the grid; the same form naming the shape set otherwise."""
+    if args.workload == "grid" and not args.shapes:
+        return METRIC
+    name = "custom shapes" if args.shapes else args.workload
+    return METRIC.replace("96-shape FP16 grid", f"{count}-shape FP16 {name}")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -410,7 +418,7 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
         e2e_value = world * total_flops / (t[1].item() / 1e3) / 1e12
 
     result: dict[str, object] = {
-        "metric": METRIC,
+        "metric": _metric(args, len(workloads)),
         "value": round(value, 3),
         "unit": "TFLOP/s",
         "n_gpus": world,
@@ -829,7 +837,7 @@ def run_reference(args: argparse.Namespace) -> dict[str, object] | None:
     base = samples[0]
     return {
         "impl": "reference",
-        "metric": METRIC,
+        "metric": _metric(args, len(workloads)),
         "value": value,
         "unit": "TFLOP/s",
         "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
