@@ -173,10 +173,13 @@ def _make_operands(workloads, device, seed_base: int):
 
 
 def _kernel_family(candidate) -> str:
-    """Roofline family of a candidate: its launch family, with the 256 x 512 pair tile apart."""
+    """Roofline family of a candidate: its launch family, with the 256 x 512 pair tile and the
+    128-deep 256 x 256 pair tile apart."""
     config = candidate.config
     if candidate.family == "pair" and config.block_n == 512:
         return "pair_wide"
+    if candidate.family == "pair" and config.block_n == 256 and config.block_k == 128:
+        return "pair_deep_k"
     return candidate.family
 
 
@@ -392,6 +395,7 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
         "stream": "stream_cluster_kernel (in-cluster split-K)",
         "pair": "pair_gemm_kernel (cta_group::2)",
         "pair_wide": "pair_gemm_kernel<512, 64> (cta_group::2, 256 x 512 tiles)",
+        "pair_deep_k": "pair_gemm_kernel<256, 128> (cta_group::2, 256 x 256 tiles, 128-deep K blocks)",
     }[dominant]
     roofline.update(_traffic_from_profiles(dominant))
 

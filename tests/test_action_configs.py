@@ -260,8 +260,9 @@ def test_pair_stream_k_rule() -> None:
     assert pair_stream_k_tiles(3, 5, 74) == 0  # under two K blocks per pair
     w = Workload(2048, 4096, 4096, "x", "y", "z")
     assert any(c.key.endswith("-streamk") for c in pair_candidates_for(w))
+    assert "pair:pair-m256n256k128-w4s3g8-streamk" in {c.key for c in pair_candidates_for(w)}
     # 32 x 37 tiles of 256 x 256 are 16 whole waves
-    assert "pair:pair-m256n256k64-w4s6g8-streamk" not in {c.key for c in pair_candidates_for(replace(w, m=8192, n=9472))}
+    assert "pair:pair-m256n256k128-w4s3g8-streamk" not in {c.key for c in pair_candidates_for(replace(w, m=8192, n=9472))}
 
 
 def test_wide_pair_candidates_need_well_filled_waves() -> None:

@@ -51,7 +51,8 @@ def test_metric_name_is_baselines_for_the_grid_only() -> None:
 def test_kernel_families() -> None:
     assert bench._kernel_family(PAIR_WIDE) == "pair_wide"
     assert bench._kernel_family(PAIR_WIDE_STREAM_K) == "pair_wide"
-    assert bench._kernel_family(PAIR_DEEP_K) == "pair"
+    assert bench._kernel_family(PAIR_DEEP_K) == "pair_deep_k"
+    assert bench._kernel_family(PAIR_NARROW) == "pair"
     assert bench._kernel_family(ActionCandidate(StreamConfig(16, 128, 64, 4, 4, 0))) == "stream"
 
 

@@ -156,7 +156,7 @@ def test_pair_split_k(split: int, block_n: int, shape: tuple[int, int, int]) -> 
     assert torch.equal(first.view(torch.int16), launch(a, b, candidate).view(torch.int16))
 
 
-@pytest.mark.parametrize("block_n", (128, 256))
+@pytest.mark.parametrize("block_n, block_k", ((128, 64), (256, 64), (256, 128)))
 @pytest.mark.parametrize(
     "shape",
     (
@@ -169,12 +169,13 @@ def test_pair_split_k(split: int, block_n: int, shape: tuple[int, int, int]) -> 
     ),
     ids=lambda s: "x".join(map(str, s)),
 )
-def test_pair_stream_k(block_n: int, shape: tuple[int, int, int]) -> None:
+def test_pair_stream_k(block_n: int, block_k: int, shape: tuple[int, int, int]) -> None:
     m, n, k = shape
     g = torch.Generator(device="cuda").manual_seed(m + n + block_n)
     a = scaled_normal((m, k), k, g)
     b = scaled_normal((k, n), k, g)
-    candidate = ActionCandidate(PairConfig(256, block_n, 64, 4, 6, 8, PAIR_STREAM_K))
+    stages = 6 if block_k == 64 else 3
+    candidate = ActionCandidate(PairConfig(256, block_n, block_k, 4, stages, 8, PAIR_STREAM_K))
     first = launch(a, b, candidate)
     assert_gemm_parity(first, a, b)
     for _ in range(2):  # later launches see the earlier ones' publication words: never matched
