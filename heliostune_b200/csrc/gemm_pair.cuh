@@ -302,11 +302,9 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         umma_f16_pair(tmem_base + col, adesc, bdesc, S::kIdesc, (!first || kk != 0) ? 1u : 0u);
       }
     };
-    auto release_stage = [&](int st) {
-      const uint32_t own_empty = smem_addr(&empty[st]);
-      umma_commit_pair(own_empty);
-      umma_commit_pair(map_to_rank(own_empty, crank | 1u));
-    };
+    // Both CTAs of the pair (cluster ranks crank and crank + 1; the leader's rank is even).
+    const uint16_t pair_mask = static_cast<uint16_t>(3u << crank);
+    auto release_stage = [&](int st) { umma_commit_pair_multicast(smem_addr(&empty[st]), pair_mask); };
     while (ok && next_segment(work, tile, kb0, kb1)) {
       if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort_flag)) {
         raise_abort(args.status, abort_flag, kStatusMmaTimeout);
@@ -371,9 +369,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         }
       }
       if (!ok) break;
-      const uint32_t own_full = smem_addr(&tmem_full[acc]);
-      umma_commit_pair(own_full);
-      umma_commit_pair(map_to_rank(own_full, crank | 1u));
+      umma_commit_pair_multicast(smem_addr(&tmem_full[acc]), pair_mask);
       if (S::kWide) {
         acc_phase ^= 1u;
       } else if (++acc == 2) {

@@ -517,6 +517,16 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t cluster_addr) {
       : "memory");
 }
 
+// umma_commit_pair onto the mbarrier at the same shared-memory offset `bar` in every CTA of
+// `cta_mask` (bit i = cluster rank i), with one instruction.
+__device__ __forceinline__ void umma_commit_pair_multicast(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
+
 // ------------------------------------------------------------------------------------------
 // UMMA descriptors
 // ------------------------------------------------------------------------------------------
