@@ -8,8 +8,8 @@
 //   * both CTAs' TMA loads complete on the leader CTA's (rank 0) stage barrier;
 //   * one thread of the leader issues the UMMAs; they read A and B from both CTAs' shared
 //     memory and accumulate rows 128r..128r+127 in CTA r's TMEM;
-//   * the leader's tcgen05.commit releases each stage in both CTAs (one commit per CTA) and
-//     publishes each finished accumulator to both CTAs' epilogues;
+//   * the leader's tcgen05.commit releases each stage in both CTAs (one commit, multicast onto
+//     both CTAs' barriers) and publishes each finished accumulator to both CTAs' epilogues;
 //   * each CTA drains its own 128 rows x BN columns exactly like the single-SM kernel, and its
 //     epilogue warps report a free accumulator on the leader's barrier.
 // The kernel is persistent: cluster p walks tiles p, p + #pairs, ... in the grouped raster, with
