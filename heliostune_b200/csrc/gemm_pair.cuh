@@ -285,12 +285,12 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     bool ok = true;
     PairWork work(args, sk_tiles, pair, pairs);
     int tile, kb0, kb1;
-    // UMMAs of one K block of stage `st` into accumulator columns [col, col + kUmmaN); B atoms
-    // from `b_atom` on. `first`: the segment's first K block (overwrite instead of accumulate).
     // Stage 0's A and B descriptors at K step 0. Any other operand's descriptor adds its byte
     // offset / 16 to the start-address field (bits 0-13; shared memory stays below 256 KB).
     const uint64_t a_desc0 = smem_desc(smem_addr(ring), 16, 1024);
     const uint64_t b_desc0 = smem_desc(smem_addr(ring) + S::kABytes, S::kBBoxBytes, 1024);
+    // UMMAs of one K block of stage `st` into accumulator columns [col, col + kUmmaN); B atoms
+    // from `b_atom` on. `first`: the segment's first K block (overwrite instead of accumulate).
     auto issue = [&](int st, uint32_t col, int b_atom, bool first) {
       const uint64_t a_st = a_desc0 + static_cast<uint64_t>(st * (S::kStageBytes >> 4));
       const uint64_t b_st = b_desc0 + static_cast<uint64_t>(st * (S::kStageBytes >> 4) +
