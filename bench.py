@@ -312,6 +312,7 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
     if args.confirm > 1 and not (args.force or args.choices):
         finalists = {w.key: _finalists(tuning.probes[w.key], args.confirm, args.confirm_within) for w in workloads}
         samples = {w.key: [[] for _ in finalists[w.key]] for w in workloads}
+        failed: set[tuple[str, int]] = set()  # a finalist that raises drops out (the probe passed)
         if world > 1:
             dist.barrier()
         for rnd in range(6):  # the first pass warms up
@@ -324,7 +325,10 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
                     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     flush.zero_()
                     start.record()
-                    launch(a, b, finalists[w.key][f])
+                    try:
+                        launch(a, b, finalists[w.key][f])
+                    except (ValueError, RuntimeError):
+                        failed.add((w.key, f))
                     end.record()
                     events.append((w.key, f, start, end))
             torch.cuda.synchronize()
@@ -334,7 +338,11 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
         if world > 1:
             dist.barrier()
         for w in workloads:
-            medians = [statistics.median(t) for t in samples[w.key]]
+            medians = [
+                math.inf if (w.key, f) in failed else statistics.median(t) for f, t in enumerate(samples[w.key])
+            ]
+            if min(medians) == math.inf:
+                continue  # keep the bandit's recommendation
             best = finalists[w.key][medians.index(min(medians))]
             confirmed += best.key != chosen[w.key].key
             chosen[w.key] = best
