@@ -886,7 +886,7 @@ def main() -> None:
     parser.add_argument("--cpu-rows", type=int, default=64)
     parser.add_argument("--cpu-budget-s", type=float, default=20.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
-    parser.add_argument("--detail", action="store_true", help="write per-shape results under gpurun_out/")
+    parser.add_argument("--detail", action="store_true", help="also write per-shape results to bench_detail_<tag>.json")
     parser.add_argument("--choices", default=None, help="per-shape choices from an earlier --detail file")
     parser.add_argument("--skip-cublas", action="store_true", help="profiling runs: no cuBLAS passes")
     parser.add_argument("--force", default=None, help="profiling runs: one candidate key for every shape")
