@@ -31,7 +31,7 @@ from heliostune_b200.action_configs import (
 )
 from heliostune_b200.configs import DEFAULT_CONFIGS, HopperGemmConfig, KernelConfig, Workload
 from heliostune_b200.hopper_kernel import hopper_matmul
-from heliostune_b200.kernel import _stream, _validate, _within_tolerance, _workspace, matmul
+from heliostune_b200.kernel import _device_guard, _stream, _validate, _within_tolerance, _workspace, matmul
 from heliostune_b200.timing import do_bench
 
 
@@ -51,7 +51,7 @@ def _split_k_matmul(a: torch.Tensor, b: torch.Tensor, config: SplitKConfig) -> t
         config.split_k,
     )
     workspace, ws_ptr, ws_bytes = _workspace(native, a, b, m, n, k)
-    with torch.cuda.device(a.device):
+    with _device_guard(a.device):
         _native.check(
             _native.library().hst_matmul_split_k(
                 config.block_m,
@@ -98,7 +98,7 @@ def _stream_matmul(a: torch.Tensor, b: torch.Tensor, config: StreamConfig) -> to
         config.split_k,
     )
     workspace, ws_ptr, ws_bytes = _workspace(native, a, b, m, n, k)
-    with torch.cuda.device(a.device):
+    with _device_guard(a.device):
         _native.check(
             _native.library().hst_matmul_stream(
                 config.block_m,
@@ -140,7 +140,7 @@ def _pair_matmul(a: torch.Tensor, b: torch.Tensor, config: PairConfig) -> torch.
         config.split_k,
     )
     workspace, ws_ptr, ws_bytes = _workspace(native, a, b, m, n, k)
-    with torch.cuda.device(a.device):
+    with _device_guard(a.device):
         _native.check(
             _native.library().hst_matmul_pair(
                 config.block_n,

@@ -18,6 +18,7 @@ import torch.distributed as dist
 
 from heliostune_b200 import _native
 from heliostune_b200.action_configs import ActionCandidate, PairConfig
+from heliostune_b200.kernel import _device_guard, _stream
 
 #: The GEMM configurations a rank uses for its slice (large M, wide N): CTA-pair 256 x 256
 #: tiles, or 256 x 512 tiles (a quarter fewer L2-to-SM bytes per FLOP, about 7% faster per FLOP
@@ -79,7 +80,7 @@ def assemble_columns(gathered: torch.Tensor, out: torch.Tensor | None = None) ->
         out = torch.empty((rows, parts * cols), dtype=torch.float16, device=gathered.device)
     if out.shape != (rows, parts * cols) or out.stride(1) != 1:
         raise ValueError("out must be [rows, parts * cols] with unit column stride")
-    with torch.cuda.device(gathered.device):
+    with _device_guard(gathered.device):
         _native.check(
             _native.library().hst_column_assemble(
                 gathered.data_ptr(),
@@ -88,7 +89,7 @@ def assemble_columns(gathered: torch.Tensor, out: torch.Tensor | None = None) ->
                 rows,
                 cols,
                 out.stride(0),
-                torch.cuda.current_stream(gathered.device).cuda_stream,
+                _stream(gathered.device),
             )
         )
     return out
@@ -184,7 +185,7 @@ class FusedColumnParallel:
                 m,
                 self.shard.n_total,
                 k,
-                torch.cuda.current_stream(self.device).cuda_stream,
+                _stream(self.device),
             )
         )
         if phase_events:

@@ -16,7 +16,7 @@ import torch
 
 from heliostune_b200 import _native
 from heliostune_b200.action_configs import ActionCandidate
-from heliostune_b200.kernel import _stream
+from heliostune_b200.kernel import _device_guard, _stream
 
 DEFAULT_EPS = 1e-6
 
@@ -33,7 +33,7 @@ def rmsnorm(x: torch.Tensor, gamma: torch.Tensor, eps: float = DEFAULT_EPS) -> t
         raise ValueError("rmsnorm needs unit-stride rows and a contiguous gamma")
     rows, hidden = int(x.shape[0]), int(x.shape[1])
     y = torch.empty((rows, hidden), device=x.device, dtype=torch.float16)
-    with torch.cuda.device(x.device):
+    with _device_guard(x.device):
         _native.check(
             _native.library().hst_rmsnorm(
                 x.data_ptr(),
@@ -104,7 +104,7 @@ def rmsnorm_matmul(
     m, k = int(x.shape[0]), int(x.shape[1])
     n = int(w.shape[1])
     out = torch.empty((m, n), device=x.device, dtype=torch.float16)
-    with torch.cuda.device(x.device):
+    with _device_guard(x.device):
         _native.check(
             _native.library().hst_rmsnorm_matmul_stream(
                 config.block_m,

@@ -13,7 +13,7 @@ import torch
 
 from heliostune_b200 import _native
 from heliostune_b200.configs import TENSOR_DESCRIPTOR_ALIGNMENT, HopperGemmConfig
-from heliostune_b200.kernel import _stream, _validate
+from heliostune_b200.kernel import _device_guard, _stream, _validate
 
 
 def hopper_matmul(a: torch.Tensor, b: torch.Tensor, config: HopperGemmConfig) -> torch.Tensor:
@@ -27,7 +27,7 @@ def hopper_matmul(a: torch.Tensor, b: torch.Tensor, config: HopperGemmConfig) ->
             f"K={k} and N={n} must both be multiples of {TENSOR_DESCRIPTOR_ALIGNMENT}"
         )
     output = torch.empty((m, n), device=a.device, dtype=torch.float16)
-    with torch.cuda.device(a.device):
+    with _device_guard(a.device):
         _native.check(
             _native.library().hst_matmul_persistent(
                 config.block_m,

@@ -9,6 +9,7 @@ kernel; there is no other implementation to fall back to.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 from typing import Any
 
@@ -31,36 +32,58 @@ def _validate(a: torch.Tensor, b: torch.Tensor) -> tuple[int, int, int]:
     return int(a.shape[0]), int(b.shape[1]), int(a.shape[1])
 
 
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """The device's current CUDA stream as a raw handle."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    if _RAW_STREAM is not None:
+        return _RAW_STREAM(index)
+    return torch.cuda.current_stream(index).cuda_stream
+
+
+def _device_guard(device: torch.device) -> contextlib.AbstractContextManager[Any]:
+    """Make ``device`` current for a launch; nothing to do when it already is."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
+
+
+#: Workspace sizes by everything the native planner reads: the config, the operands' strides and
+#: 16-byte alignment, the shape and the device. Bounded; cleared when full.
+_WORKSPACE_SIZES: dict[tuple[Any, ...], int] = {}
+_WORKSPACE_CACHE_LIMIT = 4096
 
 
 def _workspace(
     config: _native.GemmConfig, a: torch.Tensor, b: torch.Tensor, m: int, n: int, k: int
 ) -> tuple[torch.Tensor | None, int, int]:
     """Allocate (per call, as the reference) the workspace the native planner asks for."""
-    lib = _native.library()
-    size = ctypes.c_size_t(0)
-    _native.check(
-        lib.hst_gemm_workspace_size(
-            ctypes.byref(config),
-            a.data_ptr(),
-            a.stride(0),
-            a.stride(1),
-            b.data_ptr(),
-            b.stride(0),
-            b.stride(1),
-            m,
-            n,
-            k,
-            a.device.index if a.device.index is not None else torch.cuda.current_device(),
-            ctypes.byref(size),
+    device = a.device.index if a.device.index is not None else torch.cuda.current_device()
+    a_ptr, b_ptr = a.data_ptr(), b.data_ptr()
+    key = (
+        config.family, config.block_m, config.block_n, config.block_k, config.num_warps,
+        config.num_stages, config.group_m, config.split_k, a_ptr & 15, a.stride(0), a.stride(1),
+        b_ptr & 15, b.stride(0), b.stride(1), m, n, k, device,
+    )  # fmt: skip
+    nbytes = _WORKSPACE_SIZES.get(key)
+    if nbytes is None:
+        size = ctypes.c_size_t(0)
+        _native.check(
+            _native.library().hst_gemm_workspace_size(
+                ctypes.byref(config), a_ptr, a.stride(0), a.stride(1), b_ptr, b.stride(0), b.stride(1),
+                m, n, k, device, ctypes.byref(size),
+            )  # fmt: skip
         )
-    )
-    if size.value == 0:
+        nbytes = size.value
+        if len(_WORKSPACE_SIZES) >= _WORKSPACE_CACHE_LIMIT:
+            _WORKSPACE_SIZES.clear()
+        _WORKSPACE_SIZES[key] = nbytes
+    if nbytes == 0:
         return None, 0, 0
-    buffer = torch.empty(size.value, device=a.device, dtype=torch.uint8)
-    return buffer, buffer.data_ptr(), size.value
+    buffer = torch.empty(nbytes, device=a.device, dtype=torch.uint8)
+    return buffer, buffer.data_ptr(), nbytes
 
 
 def matmul(a: torch.Tensor, b: torch.Tensor, config: KernelConfig) -> torch.Tensor:
@@ -78,7 +101,7 @@ def matmul(a: torch.Tensor, b: torch.Tensor, config: KernelConfig) -> torch.Tens
         0,
     )
     workspace, ws_ptr, ws_bytes = _workspace(native, a, b, m, n, k)
-    with torch.cuda.device(a.device):
+    with _device_guard(a.device):
         _native.check(
             _native.library().hst_matmul_tile(
                 config.block_m,

@@ -254,6 +254,26 @@ def test_pair_family_with_strided_operands_and_deep_k() -> None:
         assert_gemm_parity(launch(a, b, ActionCandidate(config)), a, b)
 
 
+def test_cached_workspace_sizes_follow_operand_alignment() -> None:
+    # The host caches the planner's workspace size per config, shape, strides and 16-byte
+    # alignment: an unaligned A (a one-element offset into a larger buffer) needs the packing
+    # workspace, the aligned one does not, and alternating them must keep both exact.
+    from heliostune_b200.kernel import _WORKSPACE_SIZES
+
+    g = torch.Generator(device="cuda").manual_seed(11)
+    m, n, k = 512, 1024, 1024
+    base = scaled_normal((m * k + 8,), k, g)
+    aligned = base[: m * k].view(m, k)
+    unaligned = base[1 : m * k + 1].view(m, k)
+    b = scaled_normal((k, n), k, g)
+    candidate = ActionCandidate(PairConfig(256, 256, 128, 4, 3, 8))
+    _WORKSPACE_SIZES.clear()
+    for a in (aligned, unaligned, aligned, unaligned):
+        assert_gemm_parity(launch(a, b, candidate), a, b)
+    sizes = {key[8]: size for key, size in _WORKSPACE_SIZES.items()}  # key[8]: A's address mod 16
+    assert sizes[0] == 0 and sizes[2] > 0
+
+
 def _abi_gemm(config: _native.GemmConfig, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """Call hst_gemm of the C ABI directly with device buffers."""
     lib = _native.library()
