@@ -823,29 +823,19 @@ int check_problem(const void* a, const void* b, const void* c, int64_t m, int64_
   return HST_OK;
 }
 
-int gemm_impl(const hst_gemm_config* cfg, const void* a, int64_t sa0, int64_t sa1, const void* b,
-              int64_t sb0, int64_t sb1, void* c, int64_t ldc, int64_t m, int64_t n, int64_t k,
-              void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  HST_TRY(check_problem(a, b, c, m, n, k, ldc));
-  DeviceState* dev = nullptr;
-  HST_TRY(device_state(&dev));
-  const View va{static_cast<const __half*>(a), m, k, sa0, sa1};
-  const View vb{static_cast<const __half*>(b), k, n, sb0, sb1};
-  Plan p;
-  HST_TRY(make_plan(cfg, va, vb, m, n, k, dev->sm_count, &p));
+// Launches a planned GEMM: zero-fills C when K is 0, packs the operands TMA cannot read in place
+// into the workspace, then runs the plan's kernels. `partials_override`, when not null, replaces
+// the workspace's split-K partials slot (the allocation-free entry point passes its fixed array).
+int run_plan(const DeviceState* dev, const Plan& p, const View& va, const View& vb, __half* cc,
+             int64_t ldc, int64_t m, int64_t n, int64_t k, uint8_t* ws, float* partials_override,
+             cudaStream_t stream) {
+  const int64_t sa0 = va.s0, sa1 = va.s1, sb0 = vb.s0, sb1 = vb.s1;
   if (m == 0 || n == 0) return HST_OK;
-  __half* cc = static_cast<__half*>(c);
   if (k == 0) {
     fill_zero_fp16_kernel<<<grid_for(m * n, dev->sm_count), 256, 0, stream>>>(cc, ldc, m, n);
     HST_CUDA(cudaGetLastError());
     return HST_OK;
   }
-  if (workspace_bytes < p.total || (p.total > 0 && workspace == nullptr))
-    return fail(HST_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu required",
-                workspace_bytes, p.total);
-  if (p.total > 0 && (reinterpret_cast<uintptr_t>(workspace) % kAlign) != 0)
-    return fail(HST_ERR_INVALID, "workspace must be %zu-byte aligned", kAlign);
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
 
   Operands o;
   o.m = static_cast<int>(m);
@@ -877,7 +867,8 @@ int gemm_impl(const hst_gemm_config* cfg, const void* a, int64_t sa0, int64_t sa
   if (p.family == HST_FAMILY_SPLIT_K) {
     o.c = cc;
     o.ldc = ldc;
-    float* partials = reinterpret_cast<float*>(ws + p.off_p);
+    float* partials = partials_override != nullptr ? partials_override
+                                                   : reinterpret_cast<float*>(ws + p.off_p);
     return dispatch_stream(*dev, p, o, partials, stream);
   }
   if (p.family == HST_FAMILY_STREAM) {
@@ -887,7 +878,7 @@ int gemm_impl(const hst_gemm_config* cfg, const void* a, int64_t sa0, int64_t sa
   }
 
   // Tile and persistent kernels store C with TMA: 16-byte aligned rows, else a padded copy.
-  const bool direct_c = !p.c_tmp && (ldc % 8 == 0) && (reinterpret_cast<uintptr_t>(c) % 16 == 0);
+  const bool direct_c = !p.c_tmp && (ldc % 8 == 0) && (reinterpret_cast<uintptr_t>(cc) % 16 == 0);
   if (direct_c) {
     o.c = cc;
     o.ldc = ldc;
@@ -911,6 +902,27 @@ int gemm_impl(const hst_gemm_config* cfg, const void* a, int64_t sa0, int64_t sa
     HST_CUDA(cudaGetLastError());
   }
   return HST_OK;
+}
+
+int gemm_impl(const hst_gemm_config* cfg, const void* a, int64_t sa0, int64_t sa1, const void* b,
+              int64_t sb0, int64_t sb1, void* c, int64_t ldc, int64_t m, int64_t n, int64_t k,
+              void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  HST_TRY(check_problem(a, b, c, m, n, k, ldc));
+  DeviceState* dev = nullptr;
+  HST_TRY(device_state(&dev));
+  const View va{static_cast<const __half*>(a), m, k, sa0, sa1};
+  const View vb{static_cast<const __half*>(b), k, n, sb0, sb1};
+  Plan p;
+  HST_TRY(make_plan(cfg, va, vb, m, n, k, dev->sm_count, &p));
+  if (m > 0 && n > 0 && k > 0) {
+    if (workspace_bytes < p.total || (p.total > 0 && workspace == nullptr))
+      return fail(HST_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu required",
+                  workspace_bytes, p.total);
+    if (p.total > 0 && (reinterpret_cast<uintptr_t>(workspace) % kAlign) != 0)
+      return fail(HST_ERR_INVALID, "workspace must be %zu-byte aligned", kAlign);
+  }
+  return run_plan(dev, p, va, vb, static_cast<__half*>(c), ldc, m, n, k,
+                  static_cast<uint8_t*>(workspace), nullptr, stream);
 }
 
 }  // namespace
@@ -1264,25 +1276,31 @@ namespace {
 constexpr size_t kNoAllocScratchFloats = size_t(4) << 20;  // 4 Mi floats = 16 MiB
 static __device__ __align__(256) float g_noalloc_partials[kNoAllocScratchFloats];
 
-float* g_noalloc_ptr[kMaxDevices] = {};
+std::atomic<float*> g_noalloc_ptr[kMaxDevices] = {};
 std::mutex g_noalloc_mutex;
 
-// Device address of the scratch array on the current device, looked up once per device.
+// Device address of the scratch array on the current device. The first call on a device looks
+// it up under the mutex; later calls read the cached address without locking.
 int noalloc_scratch(float** out) {
   int dev = 0;
   HST_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return fail(HST_ERR_INVALID, "device %d out of range", dev);
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_ptr[dev] == nullptr) {
-    void* ptr = nullptr;
-    const cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_partials);
-    if (err != cudaSuccess || ptr == nullptr) {
-      return fail(HST_ERR_CUDA, "cudaGetSymbolAddress of the split-K scratch array failed: %s",
-                  cudaGetErrorString(err));
+  float* cached = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (cached == nullptr) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    cached = g_noalloc_ptr[dev].load(std::memory_order_relaxed);
+    if (cached == nullptr) {
+      void* ptr = nullptr;
+      const cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_partials);
+      if (err != cudaSuccess || ptr == nullptr) {
+        return fail(HST_ERR_CUDA, "cudaGetSymbolAddress of the split-K scratch array failed: %s",
+                    cudaGetErrorString(err));
+      }
+      cached = static_cast<float*>(ptr);
+      g_noalloc_ptr[dev].store(cached, std::memory_order_release);
     }
-    g_noalloc_ptr[dev] = static_cast<float*>(ptr);
   }
-  *out = g_noalloc_ptr[dev];
+  *out = cached;
   return HST_OK;
 }
 
@@ -1320,15 +1338,6 @@ extern "C" int hst_matmul_split_k_noalloc(int32_t block_m, int32_t block_n, int3
   }
   float* scratch = nullptr;
   HST_TRY(noalloc_scratch(&scratch));
-  Operands o;
-  o.m = static_cast<int>(m);
-  o.n = static_cast<int>(n);
-  o.k = static_cast<int>(k);
-  o.a = va.ptr;
-  o.lda = tma_row_stride(va);
-  o.b = vb.ptr;
-  o.ldb = tma_row_stride(vb);
-  o.c = static_cast<__half*>(c);
-  o.ldc = ldc;
-  return dispatch_stream(*dev, p, o, scratch, static_cast<cudaStream_t>(stream));
+  return run_plan(dev, p, va, vb, static_cast<__half*>(c), ldc, m, n, k, nullptr, scratch,
+                  static_cast<cudaStream_t>(stream));
 }

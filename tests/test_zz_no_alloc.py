@@ -2,11 +2,13 @@
 
 Callers that cannot allocate device memory at call time (a process that reserved the whole GPU
 at start-up, or an FFI binding of the C ABI without a device allocator) use
-``hst_matmul_split_k_noalloc``: the FP32 partials live in a fixed array inside the library. This
-test calls it through the C ABI twice in a row -- the second call reuses the array the first one
-left behind -- and checks each result against ``hst_matmul_split_k`` with its caller-allocated
-workspace, within the parity tolerance of the other GEMM tests. It sits in a file of its own that
-pytest collects last.
+``hst_matmul_split_k_noalloc``: the FP32 partials live in a fixed array inside the library. Both
+entry points run the same split-K kernel and the same fixed-order reduction, so their outputs
+must agree bit for bit; each is also checked against the FP32 reference with the parity
+tolerance of the other GEMM tests. Calls come in a row on one device, so a later call finds the
+partials an earlier one left in the shared array: a 16-split call followed by a 2-split call on
+the same M x N would expose a reduction that read stale slots. The file sorts last so pytest
+collects it after every other test.
 """
 
 from __future__ import annotations
@@ -19,9 +21,6 @@ import torch
 from heliostune_b200 import _native
 
 pytestmark = pytest.mark.gpu
-
-ATOL = 1e-2
-RTOL = 1e-2
 
 
 def _operands(m: int, n: int, k: int, seed: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -75,13 +74,18 @@ def _without_allocation(a: torch.Tensor, b: torch.Tensor, split: int) -> torch.T
 def test_allocation_free_split_k_matches_the_workspace_entry_point() -> None:
     if not torch.cuda.is_available():
         pytest.skip("CUDA is unavailable")
-    # Two calls in a row on different shapes: the second finds the first one's partials in the
-    # shared array and must not be affected by them.
-    for m, n, k, split, seed in ((31, 4096, 4096, 16, 1), (7, 3584, 18944, 4, 2)):
+    from tests.gpu_helpers import assert_gemm_parity
+
+    # Calls in a row: each finds the previous call's partials in the shared array. The third
+    # repeats the second's M x N with fewer splits, so slots 2..15 still hold 16-split partials.
+    cases = ((31, 4096, 4096, 16, 1), (7, 3584, 18944, 16, 2), (7, 3584, 18944, 2, 3), (1, 4096, 4096, 4, 4))
+    for m, n, k, split, seed in cases:
         a, b = _operands(m, n, k, seed)
-        expected = _with_workspace(a, b, split).float()
-        got = _without_allocation(a, b, split).float()
-        torch.testing.assert_close(got, expected, atol=ATOL, rtol=RTOL)
+        expected = _with_workspace(a, b, split)
+        got = _without_allocation(a, b, split)
+        assert torch.equal(got.view(torch.int16), expected.view(torch.int16)), (m, n, k, split)
+        assert_gemm_parity(got, a, b)
+        assert_gemm_parity(expected, a, b)
     assert _native.status(torch.cuda.current_device()) == 0
 
 
