@@ -1,8 +1,14 @@
 """Benchmark of the B200 FP16 matmul path on the 96-shape grid (and the other configurations).
 
-Default workload ``grid`` (the configuration the headline metric is quoted on): 8 (K, N)
-projection pairs of Llama-3-8B and Qwen2.5-7B x 12 values of M, FP16 operands N(0, 1)/sqrt(K)
-from seeded generators. Flow, as the reference's protocol (bank 1 selects, bank 2 scores):
+Which configuration runs:
+
+* plain ``python bench.py`` (one process): the 96-shape grid, the configuration the headline
+  metric is quoted on; ``--workload`` picks another (decode, sweep, colpar, rmsnorm);
+* under ``torch.distributed.run`` (any number of ranks, one included): the column-parallel GEMM
+  (M=8192, K=8192, N=57344 split N-wise over the ranks, slices exchanged over NVLink), the one
+  configuration that is sharded over GPUs; the grid shapes are one-GPU problems.
+
+Grid flow, as the reference's protocol (bank 1 selects, bank 2 scores):
 
 1. tuning (untimed): the Thompson-sampling bandit probes ``--budget`` candidates per shape
    with live timed launches (every probe's output is checked against an FP32 reference);
@@ -11,15 +17,17 @@ from seeded generators. Flow, as the reference's protocol (bank 1 selects, bank 
    workspace allocated per call). Before every launch a 256 MiB write flushes L2; each launch is
    bracketed by CUDA events on the launching stream. The same passes with cuBLAS
    ``torch.matmul`` give the comparison;
-3. an end-to-end pass: host->device copies of A and B from pinned memory, the launch, and the
+3. the bank-2 output of every chosen candidate is checked against the FP32 product, beside
+   cuBLAS's error on the same inputs;
+4. an end-to-end pass: host->device copies of A and B from pinned memory, the launch, and the
    device->host copy of C, inside the events;
-4. on rank 0 at N=1, the CPU baseline: the oracle's FP32 BLAS product on a bounded sample.
+5. on rank 0 at N=1, the CPU baseline: FP16 ``torch.matmul`` on all host cores.
 
 ``value`` is the grid's aggregate TFLOP/s (total FLOPs of one pass / sum of per-shape median
-latencies), ``geomean_latency_vs_cublas`` the headline ratio. Under torchrun every rank runs the
-whole grid (replicas): value = sum over ranks' FLOPs / max over ranks' time.
+latencies), ``geomean_latency_vs_cublas`` the headline ratio.
 
-``--impl reference`` times the reference's CPU path (the oracle port) on the host cores.
+``--impl reference`` times the reference's CPU path (FP16 ``torch.matmul`` on the host cores,
+through the oracle) on the same configuration.
 """
 
 from __future__ import annotations
@@ -44,7 +52,7 @@ METRIC = "geomean latency/cuBLAS torch.matmul, 96-shape FP16 grid; TFLOP/s & % r
 
 
 def _metric(args, count: int) -> str:
-    """BASELINE's metric name for the grid; the same form naming the shape set otherwise."""
+    """The headline metric's name for the grid; the same form naming the shape set otherwise."""
     if args.workload == "grid" and not args.shapes:
         return METRIC
     name = "custom shapes" if args.shapes else args.workload
@@ -58,6 +66,50 @@ def _peaks() -> tuple[dict[str, float], str]:
         data = json.loads(path.read_text())
         return {k: float(data[k]) for k in FALLBACK_PEAKS if k in data}, "measured"
     return dict(FALLBACK_PEAKS), "fallback"
+
+
+def _distributed_launch() -> bool:
+    """Whether ``torch.distributed.run`` started this process (it sets these for every rank)."""
+    return "TORCHELASTIC_RUN_ID" in os.environ or "LOCAL_WORLD_SIZE" in os.environ
+
+
+def _config(args, workloads) -> dict[str, object]:
+    """The ``config`` object of the JSON line; both arms print the same one."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.workload == "colpar":
+        from heliostune_b200.column_parallel import column_parallel_candidate
+
+        (w,) = workloads
+        exchange = (
+            "fused: GEMM epilogue stores every tile to all ranks over NVLink"
+            if args.exchange == "fused" and world > 1
+            else "NCCL all-gather + column assembly" if world > 1 else "none (one rank holds all of N)"
+        )
+        return {
+            "workload": f"colpar M={w.m} N={w.n} K={w.k}",
+            "parallelism": f"column-parallel x{world}",
+            "gemm": column_parallel_candidate(w.m, w.n // world).key,
+            "exchange": exchange,
+            "l2": "operands larger than L2",
+        }
+    workload = f"{args.workload}: {len(workloads)} shapes" if not args.shapes else f"shapes {args.shapes}"
+    selection = f"Thompson bandit, {args.budget} probes per shape on bank-1 tensors"
+    if args.force:
+        selection = f"forced: {args.force}"
+    elif args.choices:
+        selection = f"choices of {Path(args.choices).name}"
+    elif args.confirm > 1:
+        selection += (
+            f"; the best {args.confirm} probes within {args.confirm_within:.2f}x re-timed side by side in"
+            " 5 passes on bank-1 tensors"
+        )
+    return {
+        "workload": workload,
+        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+        "l2": "256 MiB write before every launch",
+        "selection": selection + "; scored on bank-2 tensors",
+        "timing": "per-launch CUDA events on the launching stream; per-shape median over steps",
+    }
 
 
 def _workloads(name: str, shapes: str | None):
@@ -413,6 +465,9 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
         t_roof = max(w.flops / (peaks["bf16_tflops"] * 1e12), w.ideal_bytes / (peaks["hbm_gbs"] * 1e9))
         shape_frac.append(t_roof / (ms / 1e3))
 
+    # ---- 2b. parity of the scored outputs: every chosen candidate on its bank-2 tensors ---------
+    parity = _grid_parity(workloads, operands, chosen)
+
     # ---- 3. end to end through the public API with host buffers ------------------------------
     if args.e2e_steps > 0:
         e2e_ms, h2d_bytes, d2h_bytes = _e2e_pass(workloads, operands, chosen, device, args.e2e_steps)
@@ -442,22 +497,9 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
         "vs_baseline": None,
         "dtype": "f16 (fp32 accumulate)",
         "data": "synthetic: seeded N(0,1)/sqrt(K) FP16 operands",
-        "config": {
-            "workload": f"{args.workload}: {len(workloads)} shapes" if not args.shapes else f"shapes {args.shapes}",
-            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-            "l2": "256 MiB write before every launch",
-            "selection": (
-                f"Thompson bandit, {args.budget} probes per shape on bank-1 tensors"
-                + (
-                    f"; the best {args.confirm} probes within {args.confirm_within:.2f}x re-timed side by side in"
-                    f" 5 passes on bank-1 tensors ({confirmed} shapes changed)"
-                    if args.confirm > 1 and not (args.force or args.choices)
-                    else ""
-                )
-                + "; scored on bank-2 tensors"
-            ),
-            "timing": "per-launch CUDA events on the launching stream; per-shape median over steps",
-        },
+        "config": _config(args, workloads),
+        "confirm_changed_shapes": confirmed,
+        "parity": parity,
         "geomean_latency_vs_cublas": round(geomean, 4),
         "cublas_tflops": round(total_flops / (sum(cublas_ms) / 1e3) / 1e12, 3),
         "shapes_faster_than_cublas": sum(r < 1.0 for r in ratios),
@@ -477,9 +519,9 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
         "tuning_s": round(tuning_s, 1),
         "status_bits": _native.status(local_rank),
     }
-    if args.detail:
-        detail = ROOT / "gpurun_out" / f"bench_detail_{args.tag or args.workload}.json"
-        detail.parent.mkdir(exist_ok=True)
+    if args.detail and rank == 0:
+        detail = Path(args.detail)
+        detail.parent.mkdir(parents=True, exist_ok=True)
         detail.write_text(
             json.dumps(
                 {
@@ -502,20 +544,63 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
             )
         )
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(workloads, args.cpu_rows, args.cpu_budget_s)
+        baseline = CpuBaseline(workloads)
+        baseline.run(args.cpu_budget_s)
+        result["cpu_baseline"] = baseline.summary()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return result if rank == 0 else None
 
 
+def _grid_parity(workloads, operands, chosen) -> dict[str, object]:
+    """Check the scored (bank-2) output of every shape's chosen candidate against the FP32 product
+    (elementwise 1e-2 + 1e-2|C|, normwise 1e-2) beside cuBLAS ``torch.matmul``'s normwise error on
+    the same inputs. Raises if any shape fails the tolerance."""
+    import torch
+
+    from heliostune_b200.action_expansion import fp32_reference, launch
+
+    worst, worst_cublas, worse, failures = 0.0, 0.0, [], []
+    for w in workloads:
+        a, b = operands[w.key]
+        expected = fp32_reference(a, b)
+        scale = max(expected.abs().max().item(), 1e-30)
+        out = launch(a, b, chosen[w.key]).float()
+        err = (out - expected).abs().max().item() / scale
+        ok = bool(torch.all((out - expected).abs() <= 1e-2 + 1e-2 * expected.abs()).item()) and err <= 1e-2
+        del out
+        cublas = (torch.matmul(a, b).float() - expected).abs().max().item() / scale
+        del expected
+        worst, worst_cublas = max(worst, err), max(worst_cublas, cublas)
+        if err > cublas:
+            worse.append(f"{w.key}: {err:.3g} vs {cublas:.3g}")
+        if not ok:
+            failures.append(f"{chosen[w.key].key} on {w.key}: normwise {err:.3g}")
+    torch.cuda.empty_cache()
+    if failures:
+        raise AssertionError("parity failure on the scored tensors: " + "; ".join(failures))
+    return {
+        "status": "ok",
+        "checked": f"bank-2 output of the chosen candidate of all {len(workloads)} shapes vs the FP32 product",
+        "max_normwise": float(f"{worst:.4g}"),
+        "max_normwise_cublas": float(f"{worst_cublas:.4g}"),
+        "shapes_with_error_above_cublas": len(worse),
+        "above_cublas": worse[:8],
+    }
+
+
 def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
-    """Config 5: C[M, N] = A[M, K] B[K, N] with B split N-wise over the ranks, each rank's
-    slice computed by the B200 GEMM, NCCL all-gather of the slices, column assembly."""
+    """Config 5: C[M, N] = A[M, K] B[K, N] with B split N-wise over the ranks. Each rank's slice
+    is computed by the CTA-pair GEMM; with several ranks the slices reach every rank either from
+    the GEMM epilogue over NVLink (fused, the default) or by an NCCL all-gather and a column
+    assembly. After the timed steps each rank checks sampled rows of its full C, spanning every
+    rank's column slice, against the FP32 product of the same seeded operands."""
     import torch
     import torch.distributed as dist
 
     from heliostune_b200 import _native
+    from heliostune_b200.action_expansion import launch
     from heliostune_b200.column_parallel import ColumnShard, column_parallel_candidate, column_parallel_matmul
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -528,12 +613,12 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
     _native.library()
-    (w,) = _workloads("colpar", args.shapes)
+    workloads = _workloads("colpar", args.shapes)
+    (w,) = workloads
     shard = ColumnShard(w.n, world, rank)
-    g = torch.Generator(device=device).manual_seed(5)
-    a = (torch.randn((w.m, w.k), generator=g, device=device) / math.sqrt(w.k)).to(torch.float16)
-    g = torch.Generator(device=device).manual_seed(1000 + rank)
-    b_shard = (torch.randn((w.k, shard.cols), generator=g, device=device) / math.sqrt(w.k)).to(torch.float16)
+    a = _colpar_a(w, device)
+    b_shard = _colpar_b_slice(w, shard.cols, rank, device)
+    candidate = column_parallel_candidate(w.m, shard.cols)
 
     if args.exchange == "fused" and world > 1:
         from heliostune_b200.column_parallel import FusedColumnParallel
@@ -559,28 +644,46 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
     sampler.__enter__()
     time.sleep(0.5)
     epoch0 = time.time()
+    out = None
     for s_ in range(args.steps):
         out = step(events[s_])
-        del out
     torch.cuda.synchronize()
     epoch1 = time.time()
     sampler.__exit__(None, None, None)
     if world > 1:
         dist.barrier()
-    gemm_ms = statistics.median(e[0].elapsed_time(e[1]) for e in events)
-    gather_ms = statistics.median(e[1].elapsed_time(e[2]) for e in events)
+    phase1_ms = statistics.median(e[0].elapsed_time(e[1]) for e in events)
+    phase2_ms = statistics.median(e[1].elapsed_time(e[2]) for e in events)
     step_ms = statistics.median(e[0].elapsed_time(e[2]) for e in events)
-    times = torch.tensor([step_ms, gemm_ms, gather_ms], device=device, dtype=torch.float64)
+
+    # The slice GEMM alone (no exchange), for the GEMM-phase roofline.
+    gemm_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(4)]
+    for start, end in gemm_events:
+        start.record()
+        launch(a, b_shard, candidate)
+        end.record()
+    torch.cuda.synchronize()
+    gemm_ms = statistics.median(start.elapsed_time(end) for start, end in gemm_events[1:])
+
+    parity = _colpar_parity(w, a, out, world, shard.cols, device)
+    del out
+    times = torch.tensor([step_ms, gemm_ms, phase1_ms, phase2_ms], device=device, dtype=torch.float64)
+    checks = torch.tensor(
+        [parity["normwise"], parity["normwise_cublas"], 0.0 if parity["ok"] else 1.0], device=device, dtype=torch.float64
+    )
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    step_ms, gemm_ms, gather_ms = (float(t) for t in times.tolist())
+        dist.all_reduce(checks, op=dist.ReduceOp.MAX)
+    step_ms, gemm_ms, phase1_ms, phase2_ms = (float(t) for t in times.tolist())
+    normwise, normwise_cublas, failed = (float(t) for t in checks.tolist())
     peaks, source = _peaks()
     flops = 2.0 * w.m * w.n * w.k
     gemm_tflops = flops / world / (gemm_ms / 1e3) / 1e12
     gather_bytes = 2.0 * w.m * w.n * (world - 1) / world
-    # Roofline of the whole step: the slower of the per-GPU GEMM at the tensor peak and the
-    # all-gather bytes every GPU receives at the measured 770 GB/s peer bandwidth.
+    # Roofline of the whole step: the slower of the per-GPU GEMM at the sustained tensor peak and
+    # the bytes every GPU receives at the measured 770 GB/s peer bandwidth.
     t_roof = max(flops / world / (peaks["bf16_tflops_sustained"] * 1e12), gather_bytes / 770e9)
+    limiter = "tensor cores (slice GEMM)" if flops / world / (peaks["bf16_tflops_sustained"] * 1e12) >= gather_bytes / 770e9 else "NVLink receive bytes per GPU"
     result: dict[str, object] = {
         "metric": "column-parallel FP16 GEMM M=8192 K=8192 N=57344: TFLOP/s (whole job)",
         "value": round(flops / (step_ms / 1e3) / 1e12, 3),
@@ -594,14 +697,18 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
         "vs_baseline": None,
         "dtype": "f16 (fp32 accumulate)",
         "data": "synthetic: seeded N(0,1)/sqrt(K) FP16 operands",
-        "config": {
-            "workload": f"colpar M={w.m} N={w.n} K={w.k}",
-            "parallelism": f"column-parallel x{world}",
-            "gemm": column_parallel_candidate(w.m, shard.cols).key,
-            "l2": "operands larger than L2",
+        "config": _config(args, workloads),
+        "note": (
+            "under torch.distributed.run bench.py runs this column-parallel configuration at every rank "
+            "count, one rank included; plain `python bench.py` runs the 96-shape grid"
+        ),
+        "parity": {
+            "status": "fail" if failed else "ok",
+            "checked": f"{parity['rows']} rows of the full C on every rank (all {world} column slices) vs the FP32 product",
+            "max_normwise": float(f"{normwise:.4g}"),
+            "max_normwise_cublas": float(f"{normwise_cublas:.4g}"),
         },
         "gemm_ms": round(gemm_ms, 4),
-        "gather_ms": round(gather_ms, 4),
         "roofline": {
             "bound": "tensor",
             "achieved": round(gemm_tflops, 2),
@@ -609,25 +716,79 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
             "unit": "TFLOP/s",
             "frac": round(gemm_tflops / peaks["bf16_tflops_sustained"], 4),
             "peak_source": f"{source} (sustained)",
-            "kernel": f"pair_gemm_kernel<{column_parallel_candidate(w.m, shard.cols).config.block_n},64> (GEMM phase, per GPU)",
+            "kernel": f"pair_gemm_kernel<{candidate.config.block_n},{candidate.config.block_k}> (slice GEMM alone, per GPU)",
             "traffic": None,
         },
         "step_roofline_frac": round(t_roof / (step_ms / 1e3), 4),
-        "gather_gbs": round(gather_bytes / (gather_ms / 1e3) / 1e9, 1) if world > 1 else None,
+        "step_roofline_limiter": limiter,
+        "exchange_bytes_per_gpu": int(gather_bytes),
         "gpu_launches": (1 if fused is not None or world == 1 else 2) * args.steps,
         "clocks": sampler.summary(epoch0, epoch1),
         "status_bits": _native.status(local_rank),
     }
+    if world > 1:
+        if fused is not None:
+            result["phases_ms"] = {"barrier+fused_gemm": round(phase1_ms, 4), "trailing_barrier": round(phase2_ms, 4)}
+            result["exchange_gbs"] = round(gather_bytes / (step_ms / 1e3) / 1e9, 1)
+            result["exchange_gbs_note"] = "bytes each GPU receives / step time (the exchange overlaps the GEMM)"
+        else:
+            result["phases_ms"] = {"gemm": round(phase1_ms, 4), "all_gather+assembly": round(phase2_ms, 4)}
+            result["exchange_gbs"] = round(gather_bytes / (phase2_ms / 1e3) / 1e9, 1)
     if fused is not None:
-        result["config"]["exchange"] = "fused: GEMM epilogue stores every tile to all ranks over NVLink"
-        result["gemm_ms_note"] = "fused mode: gemm_ms = barrier + GEMM with overlapped peer stores"
         fused.close()
-    else:
-        result["config"]["exchange"] = "NCCL all-gather + column assembly"
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        baseline = CpuBaseline(workloads)
+        baseline.run(args.cpu_budget_s)
+        result["cpu_baseline"] = baseline.summary()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if failed:
+        print(json.dumps(result), flush=True) if rank == 0 else None
+        raise SystemExit("column-parallel parity failure")
     return result if rank == 0 else None
+
+
+def _colpar_a(w, device):
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(5)
+    return (torch.randn((w.m, w.k), generator=g, device=device) / math.sqrt(w.k)).to(torch.float16)
+
+
+def _colpar_b_slice(w, cols: int, q: int, device):
+    """Column slice ``q`` of B (``cols`` columns), from its own seed, so that any rank can
+    regenerate every slice."""
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(1000 + q)
+    return (torch.randn((w.k, cols), generator=g, device=device) / math.sqrt(w.k)).to(torch.float16)
+
+
+def _colpar_parity(w, a, out, world: int, cols: int, device) -> dict[str, object]:
+    """Sampled rows of the full C against the FP32 product: two rows of every 256-row tile band
+    (at offsets that move from band to band), all N columns, so every rank's slice and every
+    tile row is covered. Elementwise 1e-2 + 1e-2|C| and normwise 1e-2, plus cuBLAS's normwise
+    error on the same rows."""
+    import torch
+
+    from heliostune_b200.action_expansion import fp32_reference
+
+    b_full = torch.cat([_colpar_b_slice(w, cols, q, device) for q in range(world)], dim=1)
+    bands = -(-w.m // 256)
+    rows = sorted({min(w.m - 1, band * 256 + off) for band in range(bands) for off in ((band * 37) % 128, 128 + (band * 101) % 128)})
+    index = torch.tensor(rows, device=device)
+    a_rows = a.index_select(0, index)
+    expected = fp32_reference(a_rows, b_full)
+    scale = max(expected.abs().max().item(), 1e-30)
+    got = out.index_select(0, index).float()
+    diff = (got - expected).abs()
+    normwise = diff.max().item() / scale
+    ok = bool(torch.all(diff <= 1e-2 + 1e-2 * expected.abs()).item()) and normwise <= 1e-2 and bool(torch.isfinite(got).all().item())
+    cublas = (torch.matmul(a_rows, b_full).float() - expected).abs().max().item() / scale
+    del b_full, expected, got, diff
+    torch.cuda.empty_cache()
+    return {"ok": ok, "normwise": normwise, "normwise_cublas": cublas, "rows": len(rows)}
 
 
 def run_rmsnorm(args: argparse.Namespace) -> dict[str, object] | None:
@@ -796,57 +957,119 @@ def _e2e_pass(workloads, operands, chosen, device, steps: int):
 # ----------------------------------------------------------------------------------------------
 
 
-def cpu_baseline(workloads, max_rows: int, budget_s: float) -> dict[str, object]:
-    """The oracle's FP32 BLAS product on the host cores, on a bounded sample of each shape.
+def _cpu_model() -> str:
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for line in out.splitlines():
+            if line.lower().startswith("model name:"):
+                return line.split(":", 1)[1].strip()
+    except (OSError, subprocess.SubprocessError):
+        pass
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
-    Sample: the first ``min(M, max_rows)`` rows of A against the full B, inputs upcast from FP16
-    inside the timing; shapes are visited in grid order until ``budget_s`` of CPU time is spent.
+
+class CpuBaseline:
+    """FP16 ``torch.matmul`` of the workload's shapes on the host cores (through the oracle), with
+    ``torch.set_num_threads(os.cpu_count())``.
+
+    The work is cut into pieces: whole shapes, or blocks of ``rows`` rows of shapes taller than
+    that (each block against the full B). ``run(budget_s)`` times pieces one after another,
+    continuing where the previous call stopped and wrapping around, until ``budget_s`` seconds
+    of products are spent; a piece's latency is the median of its samples. ``summary()`` gives
+    FLOPs of the measured pieces / the sum of their median latencies: for a workload whose every
+    piece was measured, its whole-workload rate on the CPU.
     """
-    from oracle import oracle
 
-    cores = os.cpu_count() or 1
-    rng = np.random.default_rng(0)
-    flops = 0.0
-    seconds = 0.0
-    sampled = 0
-    b_cache: dict[tuple[int, int], np.ndarray] = {}
-    for w in workloads:
-        rows = min(w.m, max_rows)
-        if (w.k, w.n) not in b_cache:
-            b_cache.clear()
-            b_cache[(w.k, w.n)] = (rng.standard_normal((w.k, w.n), dtype=np.float32) / math.sqrt(w.k)).astype(np.float16)
-        b = b_cache[(w.k, w.n)]
-        a = (rng.standard_normal((rows, w.k), dtype=np.float32) / math.sqrt(w.k)).astype(np.float16)
-        t0 = time.perf_counter()
-        oracle.gemm_fp32_blas(a, b)
-        seconds += time.perf_counter() - t0
-        flops += 2.0 * rows * w.n * w.k
-        sampled += 1
-        if seconds > budget_s:
-            break
-    return {
-        "value": round(flops / seconds / 1e12, 4),
-        "unit": "TFLOP/s",
-        "cores": cores,
-        "kind": "port",
-        "sample": f"{sampled} shapes, first min(M, {max_rows}) rows each, FP16 upcast + FP32 BLAS (numpy) on {cores} host threads",
-    }
+    def __init__(self, workloads, rows: int = 2048, seed: int = 0) -> None:
+        import torch
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.workloads = tuple(workloads)
+        self.pieces = [(w, r0, min(w.m, r0 + rows)) for w in self.workloads for r0 in range(0, w.m, rows)]
+        self.samples: list[list[float]] = [[] for _ in self.pieces]
+        self.cursor = 0
+        self.seed = seed
+        self._b: dict[tuple[int, int], object] = {}
+        self._a: dict[tuple[int, int], object] = {}
+
+    def _operands(self, w, rows: int):
+        import torch
+
+        if (w.k, w.n) not in self._b:
+            g = torch.Generator().manual_seed(self.seed + 7919 * w.k + w.n)
+            self._b[(w.k, w.n)] = (torch.randn((w.k, w.n), generator=g) / math.sqrt(w.k)).to(torch.float16)
+        if (w.k, rows) not in self._a:
+            g = torch.Generator().manual_seed(self.seed + 104729 * w.k + rows)
+            self._a[(w.k, rows)] = (torch.randn((rows, w.k), generator=g) / math.sqrt(w.k)).to(torch.float16)
+        return self._a[(w.k, rows)], self._b[(w.k, w.n)]
+
+    def run(self, budget_s: float) -> None:
+        from oracle import oracle
+
+        spent = 0.0
+        while True:
+            w, r0, r1 = self.pieces[self.cursor]
+            a, b = self._operands(w, r1 - r0)
+            t0 = time.perf_counter()
+            oracle.gemm_fp16_torch_cpu(a, b)
+            dt = time.perf_counter() - t0
+            self.samples[self.cursor].append(dt)
+            spent += dt
+            self.cursor = (self.cursor + 1) % len(self.pieces)
+            if spent >= budget_s:
+                return
+
+    def summary(self) -> dict[str, object]:
+        import torch
+
+        measured = [(p, statistics.median(t)) for p, t in zip(self.pieces, self.samples, strict=True) if t]
+        flops = sum(2.0 * (r1 - r0) * w.n * w.k for (w, r0, r1), _ in measured)
+        seconds = sum(t for _, t in measured)
+        complete = len(measured) == len(self.pieces)
+        cover = (
+            f"all {len(self.pieces)} pieces"
+            if complete
+            else f"{len(measured)} of {len(self.pieces)} pieces (the rest not reached within the budget)"
+        )
+        shapes = len(self.workloads)
+        return {
+            "value": round(flops / seconds / 1e12, 4),
+            "unit": "TFLOP/s",
+            "cores": torch.get_num_threads(),
+            "os_cpu_count": os.cpu_count(),
+            "cpu_model": _cpu_model(),
+            "kind": "port",
+            "sample": (
+                f"FP16 torch.matmul on the host ({torch.get_num_threads()} threads) over the {shapes}-shape "
+                f"workload cut into shapes and 2048-row blocks; {cover} timed, median per piece; "
+                "value = their FLOPs / sum of their medians"
+            ),
+            "full_workload": complete,
+        }
 
 
 def run_reference(args: argparse.Namespace) -> dict[str, object] | None:
+    """The reference's CPU path on the same configuration: rank 0 alone (others exit at once)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
     workloads = _workloads(args.workload, args.shapes)
-    samples = []
+    baseline = CpuBaseline(workloads)
     for _ in range(args.warmup):
-        cpu_baseline(workloads, args.cpu_rows, args.cpu_budget_s / 4)
+        baseline.run(args.cpu_step_s / 4)
+    baseline.samples = [[] for _ in baseline.pieces]  # warm-up samples are not kept
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        samples.append(cpu_baseline(workloads, args.cpu_rows, args.cpu_budget_s))
+        baseline.run(args.cpu_step_s)
     wall = time.perf_counter() - t0
-    value = statistics.median(s["value"] for s in samples)
-    base = samples[0]
+    summary = baseline.summary()
+    value = summary["value"]
     return {
         "impl": "reference",
         "metric": _metric(args, len(workloads)),
@@ -857,12 +1080,13 @@ def run_reference(args: argparse.Namespace) -> dict[str, object] | None:
         "warmup": args.warmup,
         "ms_per_step": round(wall / max(args.steps, 1) * 1e3, 1),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if args.workload == "colpar" else "weak",
         "vs_baseline": None,
-        "dtype": "f16 inputs, fp32 accumulate (CPU)",
+        "dtype": "f16 in/out (CPU torch.matmul)",
         "data": "synthetic: seeded N(0,1)/sqrt(K) FP16 operands",
-        "config": {"workload": f"{args.workload}: {len(workloads)} shapes", "parallelism": "host CPU"},
-        "cpu_baseline": {**base, "value": value},
+        "config": _config(args, workloads),
+        "step_note": f"one step = {args.cpu_step_s:g} s of products over the workload's pieces, continuing round-robin",
+        "cpu_baseline": summary,
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -873,7 +1097,12 @@ def main() -> None:
     parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    parser.add_argument("--workload", choices=("grid", "sweep", "decode", "colpar", "rmsnorm"), default="grid")
+    parser.add_argument(
+        "--workload",
+        choices=("grid", "sweep", "decode", "colpar", "rmsnorm"),
+        default=None,
+        help="default: colpar when started by torch.distributed.run, else grid",
+    )
     parser.add_argument("--shapes", default=None, help="comma list of MxNxK overriding the workload")
     parser.add_argument("--budget", type=int, default=8, help="bandit probes per shape")
     parser.add_argument("--probe-ms", type=float, default=10.0)
@@ -883,14 +1112,13 @@ def main() -> None:
     parser.add_argument("--confirm-within", type=float, default=1.10, help="finalists: probe latency within this factor of the best")
     parser.add_argument("--seed", type=int, default=0)
     parser.add_argument("--e2e-steps", type=int, default=1)
-    parser.add_argument("--cpu-rows", type=int, default=64)
-    parser.add_argument("--cpu-budget-s", type=float, default=20.0)
+    parser.add_argument("--cpu-budget-s", type=float, default=25.0, help="CPU baseline of our arm: seconds of products")
+    parser.add_argument("--cpu-step-s", type=float, default=6.0, help="reference arm: seconds of products per step")
     parser.add_argument("--no-cpu-baseline", action="store_true")
-    parser.add_argument("--detail", action="store_true", help="also write per-shape results to bench_detail_<tag>.json")
+    parser.add_argument("--detail", default=None, metavar="FILE", help="also write per-shape results and the tuning record to FILE")
     parser.add_argument("--choices", default=None, help="per-shape choices from an earlier --detail file")
     parser.add_argument("--skip-cublas", action="store_true", help="profiling runs: no cuBLAS passes")
     parser.add_argument("--force", default=None, help="profiling runs: one candidate key for every shape")
-    parser.add_argument("--tag", default=None, help="name of the --detail file")
     parser.add_argument(
         "--exchange",
         choices=("fused", "nccl"),
@@ -898,6 +1126,8 @@ def main() -> None:
         help="colpar: all-gather fused into the GEMM epilogue, or NCCL all-gather + assembly",
     )
     args = parser.parse_args()
+    if args.workload is None:
+        args.workload = "colpar" if _distributed_launch() and not args.shapes else "grid"
     if args.warmup < 3 and args.impl == "ours" and not args.shapes:
         print("note: fewer than 3 warm-up passes", file=sys.stderr)
     if args.impl == "reference":

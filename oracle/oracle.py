@@ -9,7 +9,10 @@ Each function restates one piece of the reference (mottopanikeiku/heliostune):
   with TF32 off (``src/heliostune/action_expansion.py:206-211``,
   ``tests/test_action_expansion.py:29-40``): FP16 operands, exact products, FP64 sum, one
   rounding to FP32.
-* :func:`gemm_fp32_blas` -- the same value as an FP32 BLAS product; the timed CPU baseline.
+* :func:`gemm_fp32_blas` -- the same value as an FP32 BLAS product.
+* :func:`gemm_fp16_torch_cpu` -- ``torch.matmul`` of the FP16 operands on the host cores, the
+  path the reference's decode shape runs on without a GPU (the reference times ``torch.matmul``
+  as its baseline, ``src/heliostune/kernel.py:141-168``); the timed CPU baseline.
 * :func:`gemm_split_k` -- the split-K algorithm (``action_expansion.py:56-121``) in the C
   restatement ``oracle.c``.
 * :func:`rmsnorm_reference` -- ``local_executor.py:1982-1985`` without the residual.
@@ -88,6 +91,13 @@ def gemm_fp32_reference_c(a: np.ndarray, b: np.ndarray) -> np.ndarray:
 def gemm_fp32_blas(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     """``fp32(A) @ fp32(B)`` with FP32 accumulation through the host BLAS (all host threads)."""
     return a.astype(np.float32) @ b.astype(np.float32)
+
+
+def gemm_fp16_torch_cpu(a, b):  # type: ignore[no-untyped-def]
+    """``torch.matmul`` of FP16 CPU tensors on the host cores (the caller sets the thread count)."""
+    import torch
+
+    return torch.matmul(a, b)
 
 
 def gemm_split_k(a: np.ndarray, b: np.ndarray, block_k: int, splits: int) -> np.ndarray:

@@ -326,7 +326,9 @@ def rmsnorm_fixtures() -> None:
 
 
 def main() -> None:
-    root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <path of the reference checkout>")
+    root = Path(sys.argv[1])
     _stub_environment(root)
     bandit_fixtures()
     feature_fixtures()
