@@ -252,7 +252,7 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
     from heliostune_b200 import _native
     from heliostune_b200.action_configs import b200_candidates_for
     from heliostune_b200.action_expansion import fp32_reference, launch
-    from heliostune_b200.kernel import get_hardware_profile
+    from heliostune_b200.kernel import get_hardware_profile, require_b200
     from heliostune_b200.timing import do_bench, flush_buffer
     from heliostune_b200.tuner import thompson_probe
 
@@ -267,6 +267,7 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
     _native.library()  # fails loudly if the native path is missing
     hardware = get_hardware_profile("B200", device)
+    require_b200(hardware)
     sm_count = hardware.multiprocessor_count
     workloads = _workloads(args.workload, args.shapes)
     operands = _make_operands(workloads, device, seed_base=2)  # bank 2 tensors for scoring

@@ -146,6 +146,28 @@ def get_hardware_profile(gpu: str | None = None, device: torch.device | None = N
     )
 
 
+#: Compute capability of the only GPU this library is built for (sm_100a code only).
+B200_COMPUTE_CAPABILITY = (10, 0)
+
+
+def require_b200(profile: HardwareProfile) -> None:
+    """Raise ``ProtocolError`` unless ``profile`` describes a GPU this library's kernels run on.
+
+    The kernels are compiled for sm_100a alone, so the check is the compute capability (10.0);
+    the device name must also carry "B200", since a profile is part of a run's identity and other
+    10.0 parts have other memory systems and SM counts than the ones the tuner pool assumes.
+    """
+    from heliostune_b200.errors import ProtocolError
+
+    if tuple(profile.compute_capability) != B200_COMPUTE_CAPABILITY:
+        raise ProtocolError(
+            f"{profile.device_name} has compute capability {profile.compute_capability}; "
+            f"the kernels are built for {B200_COMPUTE_CAPABILITY} (sm_100a) only"
+        )
+    if "B200" not in profile.device_name.upper():
+        raise ProtocolError(f"{profile.device_name!r} is not a B200")
+
+
 def _within_tolerance(difference: Any, expected: Any, *, atol: float, rtol: float) -> bool:
     """Elementwise ``|out - ref| <= atol + rtol * |ref|`` (``kernel.py:161-168``)."""
     return bool(torch.all(difference <= (atol + rtol * torch.abs(expected))).item())

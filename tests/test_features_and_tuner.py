@@ -12,7 +12,6 @@ from heliostune_b200.action_collection import bank_order, protocol, select_final
 from heliostune_b200.action_configs import ActionCandidate, SplitKConfig, StreamConfig
 from heliostune_b200.configs import DEFAULT_CONFIGS, DEFAULT_WORKLOADS, GRID_WORKLOADS, KernelConfig
 from heliostune_b200.features import V2_FEATURE_NAMES, launch_fields, v2_joint_features
-from heliostune_b200.hardware import expectation_for_gpu, validate_hardware
 from heliostune_b200.errors import ProtocolError
 from heliostune_b200.retrieval import log_tflops_reward
 from heliostune_b200.schema import B200_PROFILE, HardwareProfile
@@ -117,7 +116,13 @@ def test_probe_orders_are_seeded_permutations() -> None:
     assert orders == probe_orders(GRID_WORKLOADS, 3, 7)
 
 
-def test_b200_hardware_expectation() -> None:
-    validate_hardware(B200_PROFILE, expectation_for_gpu("B200"))
-    with pytest.raises(ProtocolError):
-        validate_hardware(B200_PROFILE, expectation_for_gpu("H200"))
+def test_b200_hardware_check() -> None:
+    from dataclasses import replace
+
+    from heliostune_b200.kernel import require_b200
+
+    require_b200(B200_PROFILE)
+    with pytest.raises(ProtocolError, match="compute capability"):
+        require_b200(replace(B200_PROFILE, device_name="NVIDIA H200", compute_capability=(9, 0)))
+    with pytest.raises(ProtocolError, match="not a B200"):
+        require_b200(replace(B200_PROFILE, device_name="NVIDIA GB300"))
