@@ -857,6 +857,7 @@ def run_rmsnorm(args: argparse.Namespace) -> dict[str, object] | None:
                       "roofline_frac": round(t_roof / (ours / 1e3), 4)})
     geo = math.exp(sum(math.log(f) for f in fracs) / len(fracs))
     speedups = [c["eager_us"] / c["ours_us"] for c in cases]
+    residual_cases = _residual_rmsnorm_cases(device, peaks)
     return {
         "metric": "RMSNorm fp16 (eps 1e-6) standalone and feeding the QKV GEMM: geomean fraction of roofline",
         "value": round(geo, 4),
@@ -874,7 +875,81 @@ def run_rmsnorm(args: argparse.Namespace) -> dict[str, object] | None:
                    "l2": "256 MiB write before every launch", "peak_source": source},
         "geomean_speedup_vs_eager_torch": round(math.exp(sum(map(math.log, speedups)) / len(speedups)), 3),
         "cases": cases,
+        "residual_rmsnorm": residual_cases,
     }
+
+
+def _residual_rmsnorm_cases(device, peaks) -> list[dict[str, object]]:
+    """The reference's own residual RMSNorm (BF16, 128 x 4096, z = x + r, eps 1e-5) through its
+    four entry points. ``call_us``: per-call latency with the reference's protocol (CUDA events
+    around each call from the host, L2 flushed before it), comparable with its published H100
+    medians; ``device_us``: kernel time alone, from a CUDA graph of 20 (flush, call) pairs minus
+    a graph of the 20 flushes."""
+    import torch
+
+    from heliostune_b200.fusion import RESIDUAL_RMSNORM_ENTRYPOINTS, load_residual_rmsnorm
+    from heliostune_b200.timing import do_bench, flush_buffer
+
+    g = torch.Generator(device=device).manual_seed(17)
+    x = torch.randn((128, 4096), generator=g, device=device).to(torch.bfloat16)
+    r = torch.randn((128, 4096), generator=g, device=device).to(torch.bfloat16)
+    gamma = (1.0 + 0.02 * torch.randn((4096,), generator=g, device=device)).to(torch.bfloat16)
+    flush = flush_buffer(device)
+
+    def eager():
+        z = x.float() + r.float()
+        ms = torch.mean(z * z, dim=-1, keepdim=True, dtype=torch.float32)
+        return (z * torch.rsqrt(ms + 1e-5) * gamma.float()).to(torch.bfloat16)
+
+    def graph_us(fn) -> float:
+        reps = 20
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):  # warm the allocator before capture
+            fn()
+        torch.cuda.current_stream(device).wait_stream(side)
+        torch.cuda.synchronize(device)
+        both, flushes = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(both):
+            for _ in range(reps):
+                flush.zero_()
+                fn()
+        with torch.cuda.graph(flushes):
+            for _ in range(reps):
+                flush.zero_()
+        times = []
+        for graph in (both, flushes):
+            samples = []
+            for _ in range(7):
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record()
+                graph.replay()
+                end.record()
+                torch.cuda.synchronize(device)
+                samples.append(start.elapsed_time(end))
+            times.append(statistics.median(samples[2:]))
+        del both, flushes
+        return (times[0] - times[1]) / reps * 1e3
+
+    nbytes = 3 * 128 * 4096 * 2 + 4096 * 2
+    out = []
+    for name in RESIDUAL_RMSNORM_ENTRYPOINTS:
+        fn = load_residual_rmsnorm(name)
+        call_us = do_bench(lambda: fn(x, r, gamma), quantiles=(0.5,))[0] * 1e3
+        device_us = graph_us(lambda: fn(x, r, gamma))
+        out.append({
+            "entrypoint": name,
+            "call_us": round(call_us, 2),
+            "device_us": round(device_us, 2),
+            "device_gbs": round(nbytes / (device_us / 1e6) / 1e9, 1),
+            "device_hbm_frac": round(nbytes / (device_us / 1e6) / 1e9 / peaks["hbm_gbs"], 4),
+        })
+    out.append({
+        "entrypoint": "eager torch (the reference's formula)",
+        "call_us": round(do_bench(eager, quantiles=(0.5,))[0] * 1e3, 2),
+        "device_us": round(graph_us(eager), 2),
+    })
+    return out
 
 
 def _traffic_from_profiles(family: str) -> dict[str, object]:

@@ -55,6 +55,7 @@ EXPORTED_SYMBOLS = (
     "hst_matmul_stream",
     "hst_matmul_pair",
     "hst_rmsnorm",
+    "hst_residual_rmsnorm",
     "hst_status",
     "hst_probe_wait_timeout",
     "hst_matmul_split_k_noalloc",
@@ -151,6 +152,10 @@ def _declare(lib: ctypes.CDLL) -> None:
         ),
         "hst_rmsnorm": (
             [_ptr, _i64, _ptr, _ptr, _i64, _i64, _i64, ctypes.c_float, _ptr],
+            ctypes.c_int,
+        ),
+        "hst_residual_rmsnorm": (
+            [_ptr, _i64, _ptr, _i64, _ptr, _ptr, _i64, _i64, _i64, ctypes.c_float, _i32, _ptr],
             ctypes.c_int,
         ),
         "hst_status": ([ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int], ctypes.c_int),

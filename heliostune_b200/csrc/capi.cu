@@ -1157,6 +1157,50 @@ int hst_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* y, int64_t 
   return HST_OK;
 }
 
+int hst_residual_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr,
+                         const void* gamma, void* y, int64_t ldy, int64_t rows, int64_t hidden,
+                         float eps, int32_t num_warps, void* stream) {
+  if (rows < 0 || hidden < 1) return fail(HST_ERR_INVALID, "rows must be >= 0 and hidden >= 1");
+  if (rows > INT32_MAX || hidden > INT32_MAX) return fail(HST_ERR_INVALID, "extent too large");
+  if (ldx < hidden || ldr < hidden || ldy < hidden)
+    return fail(HST_ERR_INVALID, "row strides must be >= hidden");
+  if (!(eps >= 0.f)) return fail(HST_ERR_INVALID, "eps must be non-negative");
+  if (num_warps < 1 || num_warps > 32)
+    return fail(HST_ERR_INVALID, "num_warps %d outside 1..32", num_warps);
+  if (rows == 0) return HST_OK;
+  if (x == nullptr || residual == nullptr || gamma == nullptr || y == nullptr)
+    return fail(HST_ERR_INVALID, "null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const auto* xp = static_cast<const __nv_bfloat16*>(x);
+  const auto* rp = static_cast<const __nv_bfloat16*>(residual);
+  const auto* gp = static_cast<const __nv_bfloat16*>(gamma);
+  auto* yp = static_cast<__nv_bfloat16*>(y);
+  const int threads = num_warps * 32;
+  const int h = static_cast<int>(hidden);
+  const bool aligned = hidden % 8 == 0 && ldx % 8 == 0 && ldr % 8 == 0 && ldy % 8 == 0 &&
+                       (reinterpret_cast<uintptr_t>(x) % 16) == 0 &&
+                       (reinterpret_cast<uintptr_t>(residual) % 16) == 0 &&
+                       (reinterpret_cast<uintptr_t>(gamma) % 16) == 0 &&
+                       (reinterpret_cast<uintptr_t>(y) % 16) == 0;
+  const int64_t vecs = hidden / 8;
+  const dim3 grid(static_cast<unsigned>(rows));
+  if (aligned && vecs <= int64_t(threads) * 16) {
+    int chunks = 1;
+    while (int64_t(threads) * chunks < vecs) chunks *= 2;
+    switch (chunks) {
+      case 1: residual_rmsnorm_bf16_kernel<1><<<grid, threads, 0, s>>>(xp, rp, gp, yp, h, ldx, ldr, ldy, eps); break;
+      case 2: residual_rmsnorm_bf16_kernel<2><<<grid, threads, 0, s>>>(xp, rp, gp, yp, h, ldx, ldr, ldy, eps); break;
+      case 4: residual_rmsnorm_bf16_kernel<4><<<grid, threads, 0, s>>>(xp, rp, gp, yp, h, ldx, ldr, ldy, eps); break;
+      case 8: residual_rmsnorm_bf16_kernel<8><<<grid, threads, 0, s>>>(xp, rp, gp, yp, h, ldx, ldr, ldy, eps); break;
+      default: residual_rmsnorm_bf16_kernel<16><<<grid, threads, 0, s>>>(xp, rp, gp, yp, h, ldx, ldr, ldy, eps); break;
+    }
+  } else {
+    residual_rmsnorm_bf16_scalar_kernel<<<grid, threads, 0, s>>>(xp, rp, gp, yp, h, ldx, ldr, ldy, eps);
+  }
+  HST_CUDA(cudaGetLastError());
+  return HST_OK;
+}
+
 int hst_column_assemble(const void* src, void* dst, int64_t parts, int64_t rows,
                         int64_t cols_per_part, int64_t ldd, void* stream) {
   if (parts < 1 || rows < 0 || cols_per_part < 0) return fail(HST_ERR_INVALID, "negative extent");

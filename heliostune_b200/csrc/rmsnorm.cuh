@@ -7,6 +7,8 @@
 // The row sum is a warp-shuffle tree then a cross-warp pass through shared memory.
 #pragma once
 
+#include <cuda_bf16.h>
+
 #include "ptx.cuh"
 
 namespace hst {
@@ -97,6 +99,97 @@ __global__ void __launch_bounds__(256) rmsnorm_scalar_kernel(const __half* __res
   const float inv = rsqrtf(total / static_cast<float>(hidden) + eps);
   for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
     y[row * ldy + i] = __float2half_rn((__half2float(xr[i]) * inv) * __half2float(gamma[i]));
+  }
+}
+
+// Residual RMSNorm in the reference's own form (_fusion_gpu.py:49-73; eager formula
+// local_executor.py:1982-1985): z = fp32(x) + fp32(r), y = bf16((z * rsqrt(mean(z^2) + eps)) *
+// gamma), BF16 in and out, FP32 row sum. One CTA per row; each thread holds CHUNKS 16-byte
+// vectors of x and of r (8 BF16 values each), both issued before the first use, so every byte
+// is read from HBM once. Needs hidden % 8 == 0, 16-byte aligned rows and
+// blockDim.x * CHUNKS * 8 >= hidden.
+__device__ __forceinline__ uint32_t pack_bf162(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+template <int CHUNKS>
+__global__ void __launch_bounds__(1024) residual_rmsnorm_bf16_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ r,
+    const __nv_bfloat16* __restrict__ gamma, __nv_bfloat16* __restrict__ y, int hidden,
+    int64_t ldx, int64_t ldr, int64_t ldy, float eps) {
+  __shared__ float scratch[32];
+  const int64_t row = blockIdx.x;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
+  const uint4* rr = reinterpret_cast<const uint4*>(r + row * ldr);
+  const uint4* gr = reinterpret_cast<const uint4*>(gamma);
+  uint4* yr = reinterpret_cast<uint4*>(y + row * ldy);
+  const int vecs = hidden >> 3;
+  uint4 xv[CHUNKS], rv[CHUNKS];
+#pragma unroll
+  for (int i = 0; i < CHUNKS; ++i) {
+    const int idx = threadIdx.x + i * blockDim.x;
+    if (idx < vecs) {
+      xv[i] = __ldcs(xr + idx);  // streamed: read exactly once
+      rv[i] = __ldcs(rr + idx);
+    }
+  }
+  float z[CHUNKS][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < CHUNKS; ++i) {
+    const int idx = threadIdx.x + i * blockDim.x;
+    if (idx < vecs) {
+      const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&xv[i]);
+      const __nv_bfloat162* rh = reinterpret_cast<const __nv_bfloat162*>(&rv[i]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 a = __bfloat1622float2(xh[j]);
+        const float2 b = __bfloat1622float2(rh[j]);
+        z[i][2 * j] = a.x + b.x;
+        z[i][2 * j + 1] = a.y + b.y;
+        ss = fmaf(z[i][2 * j], z[i][2 * j], ss);
+        ss = fmaf(z[i][2 * j + 1], z[i][2 * j + 1], ss);
+      }
+    }
+  }
+  const float total = block_sum(ss, scratch);
+  const float inv = rsqrtf(total / static_cast<float>(hidden) + eps);
+#pragma unroll
+  for (int i = 0; i < CHUNKS; ++i) {
+    const int idx = threadIdx.x + i * blockDim.x;
+    if (idx < vecs) {
+      const uint4 g = __ldg(gr + idx);
+      const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&g);
+      uint4 out;
+      uint32_t* o = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 gf = __bfloat1622float2(gh[j]);
+        o[j] = pack_bf162((z[i][2 * j] * inv) * gf.x, (z[i][2 * j + 1] * inv) * gf.y);
+      }
+      __stcs(yr + idx, out);
+    }
+  }
+}
+
+// Any hidden size and alignment: two passes over the row, scalar loads.
+__global__ void __launch_bounds__(1024) residual_rmsnorm_bf16_scalar_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ r,
+    const __nv_bfloat16* __restrict__ gamma, __nv_bfloat16* __restrict__ y, int hidden,
+    int64_t ldx, int64_t ldr, int64_t ldy, float eps) {
+  __shared__ float scratch[32];
+  const int64_t row = blockIdx.x;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    const float zi = __bfloat162float(x[row * ldx + i]) + __bfloat162float(r[row * ldr + i]);
+    ss = fmaf(zi, zi, ss);
+  }
+  const float total = block_sum(ss, scratch);
+  const float inv = rsqrtf(total / static_cast<float>(hidden) + eps);
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    const float zi = __bfloat162float(x[row * ldx + i]) + __bfloat162float(r[row * ldr + i]);
+    y[row * ldy + i] = __float2bfloat16_rn((zi * inv) * __bfloat162float(gamma[i]));
   }
 }
 

@@ -1,16 +1,25 @@
-"""RMSNorm on the B200, and the closed registry that hands it out.
+"""RMSNorm on the B200, and the closed registries that hand it out.
 
-The reference exposes its residual RMSNorm as ``torch.library`` ops named
-``heliostune_fusion_v2::residual_rmsnorm_w{4,8,16,32}`` behind a closed loader
-(``src/heliostune/fusion_kernels.py:72-93``, ``src/heliostune/_fusion_gpu.py:76-188``). This
-build measures the form without a residual: ``y = fp16((x * rsqrt(mean(x^2) + eps)) * gamma)``
-with an FP32 row sum, for any ``[rows, hidden]`` FP16 input. ``rmsnorm`` launches
-``hst_rmsnorm`` of the C-ABI library; ``load_rmsnorm`` is the registry.
+Two forms:
+
+* the reference's own residual RMSNorm, ``y = bf16((z * rsqrt(mean(z^2) + 1e-5)) * gamma)`` with
+  ``z = x + residual`` on BF16 ``(128, 4096)`` rows, registered as the ``torch.library`` op
+  ``heliostune_fusion_v2::residual_rmsnorm`` and handed out by ``load_residual_rmsnorm`` under
+  the reference's four entry-point names ``heliostune_fusion_v2::residual_rmsnorm_w{4,8,16,32}``
+  (``src/heliostune/_fusion_gpu.py:49-208``, ``src/heliostune/fusion_kernels.py:28-82``); the op
+  launches ``hst_residual_rmsnorm`` with 4, 8, 16 or 32 warps per row;
+* the FP16 form without a residual that the QKV configuration measures,
+  ``y = fp16((x * rsqrt(mean(x^2) + eps)) * gamma)``, for any ``[rows, hidden]`` input
+  (``rmsnorm``, ``hst_rmsnorm``; registry ``load_rmsnorm``), also fused into the GEMM
+  (``rmsnorm_matmul``).
+
+Both sum the squares of a row in FP32.
 """
 
 from __future__ import annotations
 
 from collections.abc import Callable
+from types import MappingProxyType
 
 import torch
 
@@ -128,6 +137,123 @@ def rmsnorm_matmul(
         )
     return out
 
+
+# ----------------------------------------------------------------------------------------------
+# The reference's residual RMSNorm
+# ----------------------------------------------------------------------------------------------
+
+#: Row shape and epsilon the reference's op is defined for (_fusion_gpu.py:76-109).
+RESIDUAL_RMSNORM_SHAPE = (128, 4096)
+RESIDUAL_RMSNORM_EPS = 1e-5
+
+
+@torch.library.custom_op("heliostune_fusion_v2::residual_rmsnorm", mutates_args=())
+def _residual_rmsnorm_op(x: torch.Tensor, residual: torch.Tensor, gamma: torch.Tensor, num_warps: int) -> torch.Tensor:
+    """``bf16((z * rsqrt(mean(z^2) + 1e-5)) * gamma)``, ``z = x + residual``, one CTA of
+    ``num_warps`` warps per row (``hst_residual_rmsnorm``)."""
+    return residual_rmsnorm(x, residual, gamma, eps=RESIDUAL_RMSNORM_EPS, num_warps=num_warps)
+
+
+@_residual_rmsnorm_op.register_fake
+def _(x: torch.Tensor, residual: torch.Tensor, gamma: torch.Tensor, num_warps: int) -> torch.Tensor:
+    return torch.empty_like(x)
+
+
+def residual_rmsnorm(
+    x: torch.Tensor,
+    residual: torch.Tensor,
+    gamma: torch.Tensor,
+    *,
+    eps: float = RESIDUAL_RMSNORM_EPS,
+    num_warps: int = 8,
+) -> torch.Tensor:
+    """Residual RMSNorm of BF16 ``[rows, hidden]`` rows on the GPU, any row count and width:
+    ``bf16((z * rsqrt(mean(z^2) + eps)) * gamma)`` with ``z = fp32(x) + fp32(residual)``. Inputs
+    are never modified; the output is allocated per call."""
+    if x.ndim != 2 or residual.shape != x.shape or gamma.ndim != 1 or gamma.shape[0] != x.shape[1]:
+        raise ValueError("residual_rmsnorm expects x and residual [rows, hidden] and gamma [hidden]")
+    if not x.dtype == residual.dtype == gamma.dtype == torch.bfloat16:
+        raise ValueError("x, residual, and gamma must have dtype torch.bfloat16")
+    if x.device.type != "cuda" or residual.device != x.device or gamma.device != x.device:
+        raise ValueError("x, residual, and gamma must be on the same CUDA device")
+    if x.stride(1) != 1 or residual.stride(1) != 1 or not gamma.is_contiguous():
+        raise ValueError("residual_rmsnorm needs unit-stride rows and a contiguous gamma")
+    rows, hidden = int(x.shape[0]), int(x.shape[1])
+    y = torch.empty((rows, hidden), device=x.device, dtype=torch.bfloat16)
+    with _device_guard(x.device):
+        _native.check(
+            _native.library().hst_residual_rmsnorm(
+                x.data_ptr(),
+                x.stride(0) if rows > 1 else hidden,
+                residual.data_ptr(),
+                residual.stride(0) if rows > 1 else hidden,
+                gamma.data_ptr(),
+                y.data_ptr(),
+                hidden,
+                rows,
+                hidden,
+                float(eps),
+                int(num_warps),
+                _stream(x.device),
+            )
+        )
+    return y
+
+
+def _validate_residual_rmsnorm_inputs(x: torch.Tensor, residual: torch.Tensor, gamma: torch.Tensor) -> None:
+    """The reference op's input contract and messages (_fusion_gpu.py:96-116)."""
+    if x.shape != RESIDUAL_RMSNORM_SHAPE or residual.shape != RESIDUAL_RMSNORM_SHAPE:
+        raise ValueError("x and residual must have shape (128, 4096)")
+    if gamma.shape != (RESIDUAL_RMSNORM_SHAPE[1],):
+        raise ValueError("gamma must have shape (4096,)")
+    if x.dtype != torch.bfloat16 or residual.dtype != torch.bfloat16 or gamma.dtype != torch.bfloat16:
+        raise ValueError("x, residual, and gamma must have dtype torch.bfloat16")
+    if not x.is_cuda or not residual.is_cuda or not gamma.is_cuda:
+        raise ValueError("x, residual, and gamma must be CUDA tensors")
+    if residual.device != x.device or gamma.device != x.device:
+        raise ValueError("x, residual, and gamma must be on the same CUDA device")
+    if not x.is_contiguous() or not residual.is_contiguous() or not gamma.is_contiguous():
+        raise ValueError("x, residual, and gamma must be contiguous")
+
+
+def _residual_rmsnorm_variant(num_warps: int) -> Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]:
+    def variant(x: torch.Tensor, residual: torch.Tensor, gamma: torch.Tensor) -> torch.Tensor:
+        _validate_residual_rmsnorm_inputs(x, residual, gamma)
+        return torch.ops.heliostune_fusion_v2.residual_rmsnorm(x, residual, gamma, num_warps)
+
+    variant.__name__ = f"residual_rmsnorm_w{num_warps}"
+    variant.__qualname__ = variant.__name__
+    return variant
+
+
+residual_rmsnorm_w4 = _residual_rmsnorm_variant(4)
+residual_rmsnorm_w8 = _residual_rmsnorm_variant(8)
+residual_rmsnorm_w16 = _residual_rmsnorm_variant(16)
+residual_rmsnorm_w32 = _residual_rmsnorm_variant(32)
+
+#: The reference's closed entry-point set (fusion_kernels.py:28-62), in its order.
+RESIDUAL_RMSNORM_ENTRYPOINTS: MappingProxyType[str, Callable[..., torch.Tensor]] = MappingProxyType(
+    {
+        "heliostune_fusion_v2::residual_rmsnorm_w4": residual_rmsnorm_w4,
+        "heliostune_fusion_v2::residual_rmsnorm_w8": residual_rmsnorm_w8,
+        "heliostune_fusion_v2::residual_rmsnorm_w16": residual_rmsnorm_w16,
+        "heliostune_fusion_v2::residual_rmsnorm_w32": residual_rmsnorm_w32,
+    }
+)
+
+
+def load_residual_rmsnorm(entrypoint: str) -> Callable[..., torch.Tensor]:
+    """Closed lookup of one of the reference's four entry points; anything else is a
+    ``ValueError`` with the reference's message (fusion_kernels.py:65-82)."""
+    try:
+        return RESIDUAL_RMSNORM_ENTRYPOINTS[entrypoint]
+    except (KeyError, TypeError) as exc:
+        raise ValueError(f"unknown residual RMSNorm entrypoint: {entrypoint!r}") from exc
+
+
+# ----------------------------------------------------------------------------------------------
+# The FP16 form's registry
+# ----------------------------------------------------------------------------------------------
 
 RMSNORM_ENTRYPOINTS: tuple[str, ...] = ("heliostune_b200::rmsnorm",)
 

@@ -13,6 +13,9 @@
  *   hst_matmul_split_k     <- heliostune.action_expansion._split_k_matmul src/heliostune/action_expansion.py:124
  *   hst_gemm               <- heliostune.action_expansion.launch          src/heliostune/action_expansion.py:176
  *   hst_rmsnorm            <- heliostune_fusion_v2::residual_rmsnorm      src/heliostune/_fusion_gpu.py:76
+ *                             (FP16 form without the residual, as BASELINE config 4 measures it)
+ *   hst_residual_rmsnorm   <- heliostune_fusion_v2::residual_rmsnorm_w{4,8,16,32}
+ *                                                                        src/heliostune/_fusion_gpu.py:49-94
  * hst_matmul_stream has no reference counterpart (B200 weight-streaming family, M <= 256).
  */
 #ifndef HELIOSTUNE_B200_H_
@@ -151,6 +154,14 @@ int hst_pair_stream_k_tiles(int64_t tiles, int64_t k_blocks, int64_t pairs, int6
  * no residual, caller-chosen eps. */
 int hst_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* y, int64_t ldy,
                 int64_t rows, int64_t hidden, float eps, void* stream);
+
+/* The reference's residual RMSNorm (_fusion_gpu.py:49-73, launched by _fusion_gpu.py:76-94):
+ * z = fp32(x) + fp32(residual), y = bf16((z * rsqrt(mean(z^2) + eps)) * gamma), BF16 in and out,
+ * FP32 row sum, one CTA of num_warps (1..32) warps per row -- the reference's w4/w8/w16/w32
+ * variants are num_warps 4/8/16/32. Row strides in elements. Inputs are never written. */
+int hst_residual_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr,
+                         const void* gamma, void* y, int64_t ldy, int64_t rows, int64_t hidden,
+                         float eps, int32_t num_warps, void* stream);
 
 /* Fused column-parallel GEMM (no reference counterpart). Rank `rank` of `world` (<= 9) holds
  * A [m, k] and its column slice B_r [k, n_total / world], both row-major contiguous. c_ranks[q]

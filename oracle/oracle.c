@@ -12,12 +12,14 @@
  *                          contiguous BK-aligned K intervals, tiles_per_split =
  *                          cdiv(cdiv(K, BK), S) (:79-80); each split accumulates in FP32; the
  *                          S partials are summed in FP32 in split order and narrowed once to FP16.
- *   hst_oracle_rmsnorm     the eager formula of src/heliostune/local_executor.py:1982-1985 without
- *                          the residual: y = cast((x * rsqrt(mean(x^2) + eps)) * gamma), the row
- *                          sum in FP64 and the output rounded to FP16 or BF16.
+ *   hst_oracle_rmsnorm     the eager formula of src/heliostune/local_executor.py:1982-1985:
+ *                          z = x + residual (FP32 sum; no residual in the FP16 form measured
+ *                          here), y = cast((z * rsqrt(mean(z^2) + eps)) * gamma), the row sum in
+ *                          FP64 and the output rounded to FP16 or BF16.
  * Conversions are IEEE round-to-nearest-even, written out from the format definitions.
  */
 #include <math.h>
+#include <stddef.h>
 #include <stdint.h>
 #include <string.h>
 
@@ -119,38 +121,38 @@ void hst_oracle_gemm_splitk(const uint16_t* a, int64_t sa0, int64_t sa1, const u
   }
 }
 
-/* y[r][:] = cast((x * rsqrt(mean(x^2) + eps)) * gamma); out_bf16 selects the output format. */
-void hst_oracle_rmsnorm(const uint16_t* x, const uint16_t* gamma, uint16_t* y, int64_t rows,
-                        int64_t hidden, double eps, int in_bf16, int out_bf16) {
+static float bf16_to_f32(uint16_t h) {
+  const uint32_t bits = (uint32_t)h << 16;
+  float f;
+  memcpy(&f, &bits, sizeof(f));
+  return f;
+}
+
+/* Element i of a row as FP32: z = x (no residual) or z = fp32(x) + fp32(residual), the sum
+ * rounded to FP32 as the reference's x.float() + residual.float() rounds it. */
+static float row_value(const uint16_t* xr, const uint16_t* rr, int64_t i, int in_bf16) {
+  const float v = in_bf16 ? bf16_to_f32(xr[i]) : f16_to_f32(xr[i]);
+  if (rr == NULL) return v;
+  return v + (in_bf16 ? bf16_to_f32(rr[i]) : f16_to_f32(rr[i]));
+}
+
+/* y[r][:] = cast((z * rsqrt(mean(z^2) + eps)) * gamma) with z = x or x + residual (residual may
+ * be NULL); out_bf16 selects the output format. */
+void hst_oracle_rmsnorm(const uint16_t* x, const uint16_t* residual, const uint16_t* gamma,
+                        uint16_t* y, int64_t rows, int64_t hidden, double eps, int in_bf16,
+                        int out_bf16) {
   for (int64_t r = 0; r < rows; ++r) {
     const uint16_t* xr = x + r * hidden;
+    const uint16_t* rr = residual == NULL ? NULL : residual + r * hidden;
     double ss = 0.0;
     for (int64_t i = 0; i < hidden; ++i) {
-      double v;
-      if (in_bf16) {
-        uint32_t bits = (uint32_t)xr[i] << 16;
-        float f;
-        memcpy(&f, &bits, sizeof(f));
-        v = f;
-      } else {
-        v = f16_to_f32(xr[i]);
-      }
+      const double v = row_value(xr, rr, i, in_bf16);
       ss += v * v;
     }
     const double inv = 1.0 / sqrt(ss / (double)hidden + eps);
     for (int64_t i = 0; i < hidden; ++i) {
-      double v, g;
-      if (in_bf16) {
-        uint32_t bits = (uint32_t)xr[i] << 16, gbits = (uint32_t)gamma[i] << 16;
-        float f, gf;
-        memcpy(&f, &bits, sizeof(f));
-        memcpy(&gf, &gbits, sizeof(gf));
-        v = f;
-        g = gf;
-      } else {
-        v = f16_to_f32(xr[i]);
-        g = f16_to_f32(gamma[i]);
-      }
+      const double v = row_value(xr, rr, i, in_bf16);
+      const double g = in_bf16 ? bf16_to_f32(gamma[i]) : f16_to_f32(gamma[i]);
       const double out = v * inv * g;
       y[r * hidden + i] = out_bf16 ? f32_to_bf16((float)out) : f64_to_f16(out);
     }

@@ -15,7 +15,7 @@ Each function restates one piece of the reference (mottopanikeiku/heliostune):
   as its baseline, ``src/heliostune/kernel.py:141-168``); the timed CPU baseline.
 * :func:`gemm_split_k` -- the split-K algorithm (``action_expansion.py:56-121``) in the C
   restatement ``oracle.c``.
-* :func:`rmsnorm_reference` -- ``local_executor.py:1982-1985`` without the residual.
+* :func:`rmsnorm_reference` -- ``local_executor.py:1982-1985``, with or without the residual.
 * :func:`within_tolerance` -- ``kernel.py:161-168``.
 
 Pinned against ``tests/golden/`` (made by ``tests/golden/make_golden.py`` from the reference's
@@ -53,7 +53,7 @@ def _library() -> ctypes.CDLL:
         lib.hst_oracle_gemm.restype = None
         lib.hst_oracle_gemm_splitk.argtypes = [p, i64, i64, p, i64, i64, p, i64, i64, i64, i64, i64]
         lib.hst_oracle_gemm_splitk.restype = None
-        lib.hst_oracle_rmsnorm.argtypes = [p, p, p, i64, i64, ctypes.c_double, ctypes.c_int, ctypes.c_int]
+        lib.hst_oracle_rmsnorm.argtypes = [p, p, p, p, i64, i64, ctypes.c_double, ctypes.c_int, ctypes.c_int]
         lib.hst_oracle_rmsnorm.restype = None
         lib.hst_oracle_f32_to_f16.argtypes = [ctypes.c_float]
         lib.hst_oracle_f32_to_f16.restype = ctypes.c_uint16
@@ -115,9 +115,10 @@ def gemm_split_k(a: np.ndarray, b: np.ndarray, block_k: int, splits: int) -> np.
 
 
 def rmsnorm_reference(
-    x: np.ndarray, gamma: np.ndarray, eps: float, *, bf16: bool = False
+    x: np.ndarray, gamma: np.ndarray, eps: float, *, bf16: bool = False, residual: np.ndarray | None = None
 ) -> np.ndarray:
-    """``cast((x * rsqrt(mean(x^2) + eps)) * gamma)`` per row, FP64 row sum.
+    """``cast((z * rsqrt(mean(z^2) + eps)) * gamma)`` per row with ``z = x`` or, given
+    ``residual``, ``z = fp32(x) + fp32(residual)``; FP64 row sum.
 
     With ``bf16`` the inputs are BF16 bit patterns (uint16) and the output is BF16 bits.
     """
@@ -126,9 +127,15 @@ def rmsnorm_reference(
     x_bits = x.view(np.uint16)
     g_bits = gamma.view(np.uint16)
     rows, hidden = x.shape
+    r_ptr = None
+    if residual is not None:
+        residual = np.ascontiguousarray(residual)
+        if residual.shape != x.shape:
+            raise ValueError("residual must have the shape of x")
+        r_ptr = residual.view(np.uint16).ctypes.data
     y = np.empty((rows, hidden), dtype=np.uint16)
     _library().hst_oracle_rmsnorm(
-        x_bits.ctypes.data, g_bits.ctypes.data, y.ctypes.data, rows, hidden, eps, int(bf16), int(bf16)
+        x_bits.ctypes.data, r_ptr, g_bits.ctypes.data, y.ctypes.data, rows, hidden, eps, int(bf16), int(bf16)
     )
     return y if bf16 else y.view(np.float16)
 

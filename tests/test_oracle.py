@@ -82,6 +82,16 @@ def test_rmsnorm_oracle_matches_the_reference_formula() -> None:
     assert np.mean(out == expected) > 0.995
 
 
+def test_residual_rmsnorm_oracle_matches_the_reference_output() -> None:
+    """With the residual (z = x + r, eps 1e-5, BF16) the oracle returns the bits the reference's
+    own function returned on the same inputs (local_executor.py:1982-1985)."""
+    data = np.load(GOLDEN / "rmsnorm_bf16.npz")
+    out = oracle.rmsnorm_reference(data["x"], data["gamma"], 1e-5, bf16=True, residual=data["residual"])
+    assert np.mean(out == data["expected"]) > 0.999
+    to_f32 = lambda v: (v.astype(np.uint32) << 16).view(np.float32)  # noqa: E731
+    assert np.all(np.abs(to_f32(out) - to_f32(data["expected"])) <= np.abs(to_f32(data["expected"])) * 2.0**-7 + 1e-30)
+
+
 def test_rmsnorm_fp16_oracle_is_the_fp64_formula() -> None:
     rng = np.random.default_rng(3)
     x = rng.standard_normal((4, 4096)).astype(np.float16)
