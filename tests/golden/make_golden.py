@@ -325,6 +325,39 @@ def rmsnorm_fixtures() -> None:
     print("wrote rmsnorm_bf16.npz")
 
 
+def collection_fixtures(root: Path) -> None:
+    """The reference's analysis script (scripts/analyze_action_expansion.py) on the pilot artifact
+    that heliostune_b200.collection writes for the synthetic measurements of
+    tests/golden/collection_fixture.py: the artifact's SHA-256 and what the analysis returned."""
+    import hashlib
+    import importlib.util
+
+    from heliostune.action_collection import collection_workloads
+
+    repo = HERE.parents[1]
+    if str(repo) not in sys.path:
+        sys.path.insert(0, str(repo))
+    from heliostune_b200.collection import dumps_strict
+    from tests.golden.collection_fixture import build
+
+    spec = importlib.util.spec_from_file_location("analyze_action_expansion", root / "scripts" / "analyze_action_expansion.py")
+    analyzer = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(analyzer)
+    data = build(Path(tempfile.mkdtemp(prefix="hst-collection-")))
+    text = dumps_strict(data)
+    summary = analyzer.analyze(json.loads(text), expected_workloads=collection_workloads(True))
+    _dump(
+        "collection_analysis.json",
+        {
+            "artifact_sha256": hashlib.sha256(text.encode()).hexdigest(),
+            "overall": summary["overall"],
+            "by_m": summary["by_m"],
+            "failure_row_count": summary["failure_row_count"],
+            "selected": {w["workload_key"]: w["selected"] for w in summary["workloads"]},
+        },
+    )
+
+
 def main() -> None:
     if len(sys.argv) != 2:
         raise SystemExit("usage: python tests/golden/make_golden.py <path of the reference checkout>")
@@ -336,6 +369,7 @@ def main() -> None:
     bandit_curve_fixtures()
     gemm_fixtures()
     rmsnorm_fixtures()
+    collection_fixtures(root)
 
 
 if __name__ == "__main__":
