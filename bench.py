@@ -795,7 +795,9 @@ def _colpar_parity(w, a, out, world: int, cols: int, device) -> dict[str, object
 def run_rmsnorm(args: argparse.Namespace) -> dict[str, object] | None:
     """Config 4: standalone RMSNorm over M in {1, 4096, 65536} x hidden in {4096, 8192}, and the
     RMSNorm feeding the (4096 -> 6144) QKV GEMM at M in {1, 128, 4096}. FP16, eps 1e-6,
-    x ~ N(0, 1), gamma ~ 1 + 0.1 N(0, 1). Compared with the same math in eager torch."""
+    x ~ N(0, 1), gamma ~ 1 + 0.1 N(0, 1). Compared with the same math in eager torch. Beside
+    them, the reference's own fusion suites: the residual RMSNorm (BF16, 128 x 4096) and the
+    gated-MLP projection with its epilogue (BF16, 11008 x 4096 weights)."""
     import torch
 
     from heliostune_b200 import _native
@@ -858,6 +860,7 @@ def run_rmsnorm(args: argparse.Namespace) -> dict[str, object] | None:
     geo = math.exp(sum(math.log(f) for f in fracs) / len(fracs))
     speedups = [c["eager_us"] / c["ours_us"] for c in cases]
     residual_cases = _residual_rmsnorm_cases(device, peaks)
+    gated_cases = _gated_mlp_cases(device, peaks)
     return {
         "metric": "RMSNorm fp16 (eps 1e-6) standalone and feeding the QKV GEMM: geomean fraction of roofline",
         "value": round(geo, 4),
@@ -876,7 +879,44 @@ def run_rmsnorm(args: argparse.Namespace) -> dict[str, object] | None:
         "geomean_speedup_vs_eager_torch": round(math.exp(sum(map(math.log, speedups)) / len(speedups)), 3),
         "cases": cases,
         "residual_rmsnorm": residual_cases,
+        "gated_mlp": gated_cases,
     }
+
+
+def _gated_mlp_cases(device, peaks) -> list[dict[str, object]]:
+    """The gated-MLP epilogue suite's case (BF16 x [8, 4096], Wg and Wu [11008, 4096]) through
+    ``fusion.gated_mlp`` (one launch), beside the reference's formula in eager torch (two FP32
+    matmuls, silu, product), each after an L2 flush. HBM-bound: the two weights are read once."""
+    import torch
+
+    from heliostune_b200.fusion import gated_mlp
+    from heliostune_b200.timing import do_bench
+
+    out = []
+    for m in (1, 8, 32, 64):
+        g = torch.Generator(device=device).manual_seed(17)
+        x = torch.randn((m, 4096), generator=g, device=device).to(torch.bfloat16)
+        gate = (torch.randn((11008, 4096), generator=g, device=device) / 64).to(torch.bfloat16)
+        up = (torch.randn((11008, 4096), generator=g, device=device) / 64).to(torch.bfloat16)
+
+        def eager():
+            return (torch.nn.functional.silu(torch.mm(x.float(), gate.float().T)) * torch.mm(x.float(), up.float().T)).to(torch.bfloat16)
+
+        def eager_bf16():
+            return (torch.nn.functional.silu(torch.mm(x, gate.T)) * torch.mm(x, up.T)).to(torch.bfloat16)
+
+        ours = do_bench(lambda: gated_mlp(x, gate, up), quantiles=(0.5,))[0]
+        nbytes = 2 * (2 * 11008 * 4096 + m * 4096 + m * 11008)
+        out.append({
+            "batch": m, "hidden": 4096, "intermediate": 11008,
+            "ours_us": round(ours * 1e3, 2),
+            "eager_fp32_us": round(do_bench(eager, quantiles=(0.5,))[0] * 1e3, 2),
+            "eager_bf16_cublas_us": round(do_bench(eager_bf16, quantiles=(0.5,))[0] * 1e3, 2),
+            "gbs": round(nbytes / (ours / 1e3) / 1e9, 1),
+            "hbm_frac": round(nbytes / (ours / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+        })
+        del x, gate, up
+    return out
 
 
 def _residual_rmsnorm_cases(device, peaks) -> list[dict[str, object]]:

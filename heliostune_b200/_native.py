@@ -56,6 +56,7 @@ EXPORTED_SYMBOLS = (
     "hst_matmul_pair",
     "hst_rmsnorm",
     "hst_residual_rmsnorm",
+    "hst_gated_mlp_stream",
     "hst_status",
     "hst_probe_wait_timeout",
     "hst_matmul_split_k_noalloc",
@@ -156,6 +157,10 @@ def _declare(lib: ctypes.CDLL) -> None:
         ),
         "hst_residual_rmsnorm": (
             [_ptr, _i64, _ptr, _i64, _ptr, _ptr, _i64, _i64, _i64, ctypes.c_float, _i32, _ptr],
+            ctypes.c_int,
+        ),
+        "hst_gated_mlp_stream": (
+            [_i32] * 4 + [_ptr, _i64, _ptr, _i64, _ptr, _i64, _ptr, _i64, _i64, _i64, _i64, _ptr],
             ctypes.c_int,
         ),
         "hst_status": ([ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int], ctypes.c_int),

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <chrono>
 #include <cstdarg>
@@ -14,6 +15,7 @@
 #include <string>
 
 #include "../../include/heliostune_b200.h"
+#include "gemm_gated.cuh"
 #include "gemm_pair.cuh"
 #include "gemm_stream.cuh"
 #include "gemm_stream_cluster.cuh"
@@ -120,7 +122,8 @@ std::once_flag g_encode_once;
 cudaError_t g_encode_error = cudaSuccess;
 
 int encode_tiled_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
-                    uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+                    uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
+                    CUtensorMapDataType type = CU_TENSOR_MAP_DATA_TYPE_FLOAT16) {
   std::call_once(g_encode_once, [] {
     cudaDriverEntryPointQueryResult q;
     g_encode_error = cudaGetDriverEntryPointByVersion(
@@ -138,7 +141,7 @@ int encode_tiled_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
   const cuuint64_t strides[1] = {row_stride_elems * 2};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t elem_strides[2] = {1, 1};
-  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base),
+  const CUresult r = g_encode(map, type, 2, const_cast<void*>(base),
                               dims, strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -806,6 +809,89 @@ int dispatch_stream_cluster(const DeviceState& dev, const Plan& p, const Operand
 }
 
 // ------------------------------------------------------------------------------------------
+// Gated-MLP weight streaming (BF16, K-major weights)
+// ------------------------------------------------------------------------------------------
+
+// A BF16 [outer, inner] row-major tensor in 128-byte-swizzled boxes.
+int encode_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                   uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+  return encode_tiled_2d(map, base, inner, outer, row_stride_elems, box_inner, box_outer,
+                         CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+}
+
+struct GatedProblem {
+  const void* x;
+  int64_t ldx;
+  const void* gate;
+  int64_t ld_gate;
+  const void* up;
+  int64_t ld_up;
+  void* out;
+  int64_t ldo;
+  int m, n, k;
+};
+
+// K splits per weight for an automatic request: of 1, 2 and 4, the most whose 2S-CTA clusters
+// still all fit one resident wave, counting how many CTAs share an SM at this shared-memory size.
+template <int MP, int BK>
+int gated_auto_splits(int n, int k, int stages, int sms) {
+  using G = GatedShape<MP, BK>;
+  const int64_t tiles = cdiv(n, G::kNT);
+  const int64_t k_blocks = cdiv(k, BK);
+  int best = 1;
+  for (int s : {2, 4}) {
+    if (k_blocks < s) break;
+    const int64_t per_sm = std::max<int64_t>(1, kSmemPerSm / (G::smem_bytes(stages, 2 * s) + kSmemReservedPerCta));
+    if (tiles * 2 * s <= per_sm * sms) best = s;
+  }
+  return best;
+}
+
+template <int MP, int BK>
+int launch_gated(const DeviceState& dev, const GatedProblem& p, int stages, int splits, cudaStream_t stream) {
+  using G = GatedShape<MP, BK>;
+  static std::atomic<uint64_t> smem_done{0};
+  HST_TRY(allow_smem(gated_stream_kernel<MP, BK>, smem_done));
+  if (stages < 2) stages = 2;
+  if (stages > kStreamMaxStages) stages = kStreamMaxStages;
+  if (splits == 0) splits = gated_auto_splits<MP, BK>(p.n, p.k, stages, dev.sm_count);
+  int kb_per_split = 0, eff = 0;
+  HST_TRY(split_plan(p.k, BK, splits, &kb_per_split, &eff));
+  while (stages > 2 && G::smem_bytes(stages, 2 * eff) > kMaxDynamicSmem) --stages;
+  if (G::smem_bytes(stages, 2 * eff) > kMaxDynamicSmem)
+    return fail(HST_ERR_UNSUPPORTED, "gated tile does not fit shared memory");
+  CUtensorMap mx, mg, mu;
+  HST_TRY(encode_bf16_2d(&mx, p.x, p.k, p.m, p.ldx, 64, MP));
+  HST_TRY(encode_bf16_2d(&mg, p.gate, p.k, p.n, p.ld_gate, 64, G::kNT));
+  HST_TRY(encode_bf16_2d(&mu, p.up, p.k, p.n, p.ld_up, 64, G::kNT));
+  GatedStreamArgs args;
+  args.m = p.m;
+  args.n = p.n;
+  args.k = p.k;
+  args.k_blocks = static_cast<int>(cdiv(p.k, BK));
+  args.kb_per_split = kb_per_split;
+  args.splits = eff;
+  args.stages = stages;
+  args.status = dev.status;
+  args.out = static_cast<__nv_bfloat16*>(p.out);
+  args.ldo = p.ldo;
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(static_cast<unsigned>(cdiv(p.n, G::kNT)), static_cast<unsigned>(2 * eff));
+  lc.blockDim = dim3(kStreamThreads);
+  lc.dynamicSmemBytes = smem_for_tmem(G::smem_bytes(stages, 2 * eff), G::kTmemCols);
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = static_cast<unsigned>(2 * eff);
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  HST_CUDA(cudaLaunchKernelEx(&lc, gated_stream_kernel<MP, BK>, mx, mg, mu, args));
+  return HST_OK;
+}
+
+// ------------------------------------------------------------------------------------------
 // Common GEMM driver
 // ------------------------------------------------------------------------------------------
 
@@ -1184,9 +1270,9 @@ int hst_residual_rmsnorm(const void* x, int64_t ldx, const void* residual, int64
                        (reinterpret_cast<uintptr_t>(y) % 16) == 0;
   const int64_t vecs = hidden / 8;
   const dim3 grid(static_cast<unsigned>(rows));
-  if (aligned && vecs <= int64_t(threads) * 16) {
-    int chunks = 1;
-    while (int64_t(threads) * chunks < vecs) chunks *= 2;
+  int chunks = 1;
+  while (chunks < 16 && int64_t(threads) * chunks < vecs) chunks *= 2;
+  if (aligned && int64_t(threads) * chunks >= vecs && threads <= residual_rmsnorm_max_threads(chunks)) {
     switch (chunks) {
       case 1: residual_rmsnorm_bf16_kernel<1><<<grid, threads, 0, s>>>(xp, rp, gp, yp, h, ldx, ldr, ldy, eps); break;
       case 2: residual_rmsnorm_bf16_kernel<2><<<grid, threads, 0, s>>>(xp, rp, gp, yp, h, ldx, ldr, ldy, eps); break;
@@ -1199,6 +1285,42 @@ int hst_residual_rmsnorm(const void* x, int64_t ldx, const void* residual, int64
   }
   HST_CUDA(cudaGetLastError());
   return HST_OK;
+}
+
+int hst_gated_mlp_stream(int32_t block_m, int32_t block_k, int32_t num_stages, int32_t split_k,
+                         const void* x, int64_t ldx, const void* w_gate, int64_t ld_gate,
+                         const void* w_up, int64_t ld_up, void* out, int64_t ldo, int64_t m,
+                         int64_t n, int64_t k, void* stream) {
+  if (m < 1 || m > 64) return fail(HST_ERR_INVALID, "the gated MLP stream kernel needs 1 <= M <= 64 (got %lld)", (long long)m);
+  if (n < 1 || k < 1 || n > INT32_MAX / 2 || k > INT32_MAX / 2) return fail(HST_ERR_INVALID, "bad N or K");
+  if (block_m == 0) block_m = m <= 16 ? 16 : (m <= 32 ? 32 : 64);
+  if ((block_m != 16 && block_m != 32 && block_m != 64) || m > block_m)
+    return fail(HST_ERR_INVALID, "block_m must be 16, 32 or 64 and at least M");
+  if (block_k != 64 && block_k != 128) return fail(HST_ERR_INVALID, "block_k must be 64 or 128");
+  if (split_k != 0 && split_k != 1 && split_k != 2 && split_k != 4)
+    return fail(HST_ERR_INVALID, "split_k must be 0 (automatic), 1, 2 or 4");
+  if (num_stages < 0 || num_stages > kStreamMaxStages) return fail(HST_ERR_INVALID, "num_stages outside 0..%d", kStreamMaxStages);
+  if (x == nullptr || w_gate == nullptr || w_up == nullptr || out == nullptr) return fail(HST_ERR_INVALID, "null pointer");
+  if (k % 8 != 0 || ldx % 8 != 0 || ld_gate % 8 != 0 || ld_up % 8 != 0 || ldx < k || ld_gate < k || ld_up < k ||
+      (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w_gate) & 15) ||
+      (reinterpret_cast<uintptr_t>(w_up) & 15))
+    return fail(HST_ERR_INVALID, "x and the weights must be row-major with 16-byte aligned rows (K and leading dimensions multiples of 8)");
+  if (ldo < n) return fail(HST_ERR_INVALID, "ldo < N");
+  DeviceState* dev = nullptr;
+  HST_TRY(device_state(&dev));
+  const GatedProblem p{x, ldx, w_gate, ld_gate, w_up, ld_up, out, ldo, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k)};
+  const int stages = num_stages == 0 ? 4 : num_stages;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define HST_GATED_CASE(MP_, BK_) \
+  if (block_m == MP_ && block_k == BK_) return launch_gated<MP_, BK_>(*dev, p, stages, split_k, s);
+  HST_GATED_CASE(16, 64)
+  HST_GATED_CASE(32, 64)
+  HST_GATED_CASE(64, 64)
+  HST_GATED_CASE(16, 128)
+  HST_GATED_CASE(32, 128)
+  HST_GATED_CASE(64, 128)
+#undef HST_GATED_CASE
+  return fail(HST_ERR_UNSUPPORTED, "no gated kernel for block_m %d, block_k %d", block_m, block_k);
 }
 
 int hst_column_assemble(const void* src, void* dst, int64_t parts, int64_t rows,

@@ -32,9 +32,9 @@ __device__ __forceinline__ float block_sum(float v, float* scratch) {
   return total;
 }
 
-// hidden % 8 == 0, 16-byte aligned rows; blockDim.x * CHUNKS * 8 >= hidden.
+// hidden % 8 == 0, 16-byte aligned rows; blockDim.x * CHUNKS * 8 >= hidden, blockDim.x <= 256.
 template <int CHUNKS>
-__global__ void __launch_bounds__(1024) rmsnorm_vec_kernel(const __half* __restrict__ x,
+__global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const __half* __restrict__ x,
                                                            const __half* __restrict__ gamma,
                                                            __half* __restrict__ y, int hidden,
                                                            int64_t ldx, int64_t ldy, float eps) {
@@ -105,16 +105,21 @@ __global__ void __launch_bounds__(256) rmsnorm_scalar_kernel(const __half* __res
 // Residual RMSNorm in the reference's own form (_fusion_gpu.py:49-73; eager formula
 // local_executor.py:1982-1985): z = fp32(x) + fp32(r), y = bf16((z * rsqrt(mean(z^2) + eps)) *
 // gamma), BF16 in and out, FP32 row sum. One CTA per row; each thread holds CHUNKS 16-byte
-// vectors of x and of r (8 BF16 values each), both issued before the first use, so every byte
-// is read from HBM once. Needs hidden % 8 == 0, 16-byte aligned rows and
-// blockDim.x * CHUNKS * 8 >= hidden.
+// vectors of x and of r (8 BF16 values each), all issued before the first use, so every byte is
+// read from HBM once; z is formed again from them for the output (the same FP32 sums). Needs
+// hidden % 8 == 0, 16-byte aligned rows, blockDim.x * CHUNKS * 8 >= hidden and blockDim.x <=
+// residual_rmsnorm_max_threads(CHUNKS).
+__host__ __device__ constexpr int residual_rmsnorm_max_threads(int chunks) {
+  return chunks >= 16 ? 256 : chunks >= 8 ? 512 : 1024;
+}
+
 __device__ __forceinline__ uint32_t pack_bf162(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
 template <int CHUNKS>
-__global__ void __launch_bounds__(1024) residual_rmsnorm_bf16_kernel(
+__global__ void __launch_bounds__(residual_rmsnorm_max_threads(CHUNKS)) residual_rmsnorm_bf16_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ r,
     const __nv_bfloat16* __restrict__ gamma, __nv_bfloat16* __restrict__ y, int hidden,
     int64_t ldx, int64_t ldr, int64_t ldy, float eps) {
@@ -134,22 +139,22 @@ __global__ void __launch_bounds__(1024) residual_rmsnorm_bf16_kernel(
       rv[i] = __ldcs(rr + idx);
     }
   }
-  float z[CHUNKS][8];
+  // z of the 8 values of chunk i, pair j: the reference's FP32 sum x + r.
+  auto z_pair = [&](int i, int j) {
+    const float2 a = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(&xv[i])[j]);
+    const float2 b = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(&rv[i])[j]);
+    return make_float2(a.x + b.x, a.y + b.y);
+  };
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < CHUNKS; ++i) {
     const int idx = threadIdx.x + i * blockDim.x;
     if (idx < vecs) {
-      const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&xv[i]);
-      const __nv_bfloat162* rh = reinterpret_cast<const __nv_bfloat162*>(&rv[i]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float2 a = __bfloat1622float2(xh[j]);
-        const float2 b = __bfloat1622float2(rh[j]);
-        z[i][2 * j] = a.x + b.x;
-        z[i][2 * j + 1] = a.y + b.y;
-        ss = fmaf(z[i][2 * j], z[i][2 * j], ss);
-        ss = fmaf(z[i][2 * j + 1], z[i][2 * j + 1], ss);
+        const float2 z = z_pair(i, j);
+        ss = fmaf(z.x, z.x, ss);
+        ss = fmaf(z.y, z.y, ss);
       }
     }
   }
@@ -165,8 +170,9 @@ __global__ void __launch_bounds__(1024) residual_rmsnorm_bf16_kernel(
       uint32_t* o = reinterpret_cast<uint32_t*>(&out);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
+        const float2 z = z_pair(i, j);
         const float2 gf = __bfloat1622float2(gh[j]);
-        o[j] = pack_bf162((z[i][2 * j] * inv) * gf.x, (z[i][2 * j + 1] * inv) * gf.y);
+        o[j] = pack_bf162((z.x * inv) * gf.x, (z.y * inv) * gf.y);
       }
       __stcs(yr + idx, out);
     }

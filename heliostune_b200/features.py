@@ -1,4 +1,4 @@
-"""The 25-column v2 feature basis of the bandit.
+"""The bandit's feature bases: the reference's 25-column v2 basis and a B200 extension.
 
 ``v2_joint_features`` restates ``_v2_values`` at ``src/heliostune/features.py:66-116`` column
 for column. The reference only defines it for tile configurations; here every family is mapped
@@ -8,6 +8,13 @@ onto the same six launch fields by :func:`launch_fields`:
 * split-K -- ``group_m`` carries ``split_k`` (the reference has no raster group for split-K);
 * stream -- ``group_m`` carries the split the launcher will actually use for the shape;
 * pair -- the fields as given (``block_m`` = 256 rows per two SMs).
+
+The v2 fields cannot tell the B200 families apart: a 256 x 256 pair tile, its split and stream-K
+forms and the 128-deep form differ in no field or in ``block_k`` alone, and a stream launch's
+split hides in ``group_m``. :func:`b200_joint_features` appends columns that name them: the
+family, the CTAs per cluster, the effective K splits and K per split, stream-K, the share of the
+B200's resident slots the launch keeps busy over its waves, and the family x log M products the
+crossovers between families follow.
 """
 
 from __future__ import annotations
@@ -18,7 +25,16 @@ from typing import NamedTuple
 import numpy as np
 from numpy.typing import NDArray
 
-from heliostune_b200.action_configs import PairConfig, SplitKConfig, StreamConfig, stream_splits
+from heliostune_b200.action_configs import (
+    PAIR_STREAM_K,
+    PairConfig,
+    SplitKConfig,
+    StreamConfig,
+    resident_clusters,
+    split_plan,
+    stream_splits,
+    wave_fill,
+)
 from heliostune_b200.configs import HopperGemmConfig, KernelConfig, Workload
 from heliostune_b200.schema import HardwareProfile
 
@@ -131,3 +147,82 @@ def v2_joint_features(
     """The 25-column feature vector of one (workload, configuration, hardware) triple."""
     fields = launch_fields(workload, config, hardware)
     return np.asarray(_v2_values(workload, fields, hardware), dtype=np.float64)
+
+
+#: The v2 columns followed by the B200 columns of :func:`b200_joint_features`.
+B200_FEATURE_NAMES: tuple[str, ...] = (
+    *V2_FEATURE_NAMES,
+    "family_persistent",
+    "family_split_k",
+    "family_stream",
+    "family_pair",
+    "cluster_ctas",
+    "k_splits",
+    "log_k_per_split",
+    "stream_k",
+    "wave_fill",
+    "stream_x_log_m",
+    "pair_x_log_m",
+    "split_k_x_log_m",
+)
+
+
+class _Launch(NamedTuple):
+    family: str
+    cluster: int  # CTAs per cluster (a CTA pair is 2)
+    splits: int  # K intervals one output tile is summed from
+    k_block: int
+    stream_k: bool
+    busy: float  # share of the resident slots busy over the launch's waves
+
+
+def _launch_shape(workload: Workload, config: object, sms: int) -> _Launch:
+    m, n, k = workload.m, workload.n, workload.k
+    if isinstance(config, PairConfig):
+        tiles = -(-m // 256) * -(-n // config.block_n)
+        splits = config.split_k if config.split_k > 1 else 1
+        cluster = 2 * splits
+        slots = resident_clusters(min(cluster, 8), sms)
+        busy = 1.0 if config.split_k == PAIR_STREAM_K else wave_fill(tiles, slots)
+        return _Launch("pair", cluster, splits, config.block_k, config.split_k == PAIR_STREAM_K, busy)
+    if isinstance(config, StreamConfig):
+        splits = stream_splits(m, n, k, config, sms)
+        ctas = -(-n // config.block_n)
+        return _Launch("stream", splits, splits, config.block_k, False, wave_fill(ctas, resident_clusters(splits, sms)))
+    if isinstance(config, SplitKConfig):
+        bk = 64 if config.block_k <= 64 else 128
+        splits = split_plan(k, bk, config.split_k)[1]
+        return _Launch("split_k", 1, splits, bk, False, wave_fill(-(-n // config.block_n) * splits, sms))
+    tiles = -(-m // config.block_m) * -(-n // config.block_n)  # type: ignore[attr-defined]
+    family = "persistent" if isinstance(config, HopperGemmConfig) else "tile"
+    return _Launch(family, 1, 1, config.block_k, False, wave_fill(tiles, sms))  # type: ignore[attr-defined]
+
+
+def b200_joint_features(
+    workload: Workload,
+    config: KernelConfig | HopperGemmConfig | SplitKConfig | StreamConfig | PairConfig,
+    hardware: HardwareProfile,
+) -> NDArray[np.float64]:
+    """The v2 vector of the same triple followed by the B200 columns (:data:`B200_FEATURE_NAMES`)."""
+    fields = launch_fields(workload, config, hardware)
+    launch = _launch_shape(workload, config, hardware.multiprocessor_count)
+    log_m = math.log2(workload.m) / 14.0
+    is_stream = float(launch.family == "stream")
+    is_pair = float(launch.family == "pair")
+    is_split = float(launch.family == "split_k")
+    k_per_split = max(1.0, workload.k / launch.splits)
+    extra = (
+        float(launch.family == "persistent"),
+        is_split,
+        is_stream,
+        is_pair,
+        math.log2(launch.cluster) / 4.0,
+        math.log2(launch.splits) / 4.0,
+        math.log2(k_per_split) / 14.0,
+        float(launch.stream_k),
+        launch.busy,
+        is_stream * log_m,
+        is_pair * log_m,
+        is_split * log_m,
+    )
+    return np.asarray((*_v2_values(workload, fields, hardware), *extra), dtype=np.float64)

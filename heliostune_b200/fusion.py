@@ -14,6 +14,10 @@ Two forms:
   (``rmsnorm_matmul``).
 
 Both sum the squares of a row in FP32.
+
+And the gated-MLP projection of the reference's epilogue suite (``gated_mlp``,
+``silu(x Wg^T) * (x Wu^T)`` in BF16, local_executor.py:1970-1979) as one weight-streaming launch
+with the activation and product in its epilogue (``hst_gated_mlp_stream``), for M <= 64.
 """
 
 from __future__ import annotations
@@ -249,6 +253,56 @@ def load_residual_rmsnorm(entrypoint: str) -> Callable[..., torch.Tensor]:
         return RESIDUAL_RMSNORM_ENTRYPOINTS[entrypoint]
     except (KeyError, TypeError) as exc:
         raise ValueError(f"unknown residual RMSNorm entrypoint: {entrypoint!r}") from exc
+
+
+# ----------------------------------------------------------------------------------------------
+# Gated-MLP projection with its epilogue
+# ----------------------------------------------------------------------------------------------
+
+#: Rows the fused gated-MLP kernel serves (the decode regime; UMMA N = M padded to 16..64).
+GATED_MLP_M_LIMIT = 64
+
+
+def gated_mlp(
+    x: torch.Tensor,
+    gate_weight: torch.Tensor,
+    up_weight: torch.Tensor,
+    *,
+    block_m: int = 0,
+    block_k: int = 64,
+    num_stages: int = 0,
+    split_k: int = 0,
+) -> torch.Tensor:
+    """``bf16(silu(x @ gate_weight.T) * (x @ up_weight.T))`` with FP32 accumulation, the gated-MLP
+    epilogue suite's operation (local_executor.py:1970-1979; shapes ``x [batch, hidden]``,
+    weights ``[intermediate, hidden]``, all BF16 row-major). One launch streams both weights
+    once; the activation and the product happen on the FP32 sums before the only rounding.
+    ``batch`` must be at most :data:`GATED_MLP_M_LIMIT`; ``hidden`` a multiple of 8."""
+    if x.ndim != 2 or gate_weight.ndim != 2 or up_weight.shape != gate_weight.shape:
+        raise ValueError("gated_mlp expects x [batch, hidden] and two weights [intermediate, hidden]")
+    if gate_weight.shape[1] != x.shape[1]:
+        raise ValueError(f"incompatible shapes: x {tuple(x.shape)} and weights {tuple(gate_weight.shape)}")
+    if not x.dtype == gate_weight.dtype == up_weight.dtype == torch.bfloat16:
+        raise ValueError("x and the weights must have dtype torch.bfloat16")
+    if x.device.type != "cuda" or gate_weight.device != x.device or up_weight.device != x.device:
+        raise ValueError("x and the weights must be on the same CUDA device")
+    if not (x.is_contiguous() and gate_weight.is_contiguous() and up_weight.is_contiguous()):
+        raise ValueError("x and the weights must be contiguous row-major tensors")
+    m, k = int(x.shape[0]), int(x.shape[1])
+    n = int(gate_weight.shape[0])
+    if not 1 <= m <= GATED_MLP_M_LIMIT:
+        raise ValueError(f"the fused gated MLP serves 1 <= batch <= {GATED_MLP_M_LIMIT}, got {m}")
+    out = torch.empty((m, n), device=x.device, dtype=torch.bfloat16)
+    with _device_guard(x.device):
+        _native.check(
+            _native.library().hst_gated_mlp_stream(
+                block_m, block_k, num_stages, split_k,
+                x.data_ptr(), k, gate_weight.data_ptr(), k, up_weight.data_ptr(), k,
+                out.data_ptr(), n, m, n, k,
+                _stream(x.device),
+            )
+        )
+    return out
 
 
 # ----------------------------------------------------------------------------------------------

@@ -16,6 +16,7 @@
  *                             (FP16 form without the residual, as BASELINE config 4 measures it)
  *   hst_residual_rmsnorm   <- heliostune_fusion_v2::residual_rmsnorm_w{4,8,16,32}
  *                                                                        src/heliostune/_fusion_gpu.py:49-94
+ *   hst_gated_mlp_stream   <- the gated-MLP epilogue suite's candidate    src/heliostune/local_executor.py:1970-1979
  * hst_matmul_stream has no reference counterpart (B200 weight-streaming family, M <= 256).
  */
 #ifndef HELIOSTUNE_B200_H_
@@ -162,6 +163,19 @@ int hst_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* y, int64_t 
 int hst_residual_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr,
                          const void* gamma, void* y, int64_t ldy, int64_t rows, int64_t hidden,
                          float eps, int32_t num_warps, void* stream);
+
+/* Gated-MLP projection with its epilogue, out = bf16(silu(x Wg^T) * (x Wu^T)), in one
+ * weight-streaming launch (replaces the two FP32 matmuls, silu and product of the reference's
+ * gated-MLP epilogue suite, local_executor.py:1970-1979). BF16 x [m, k] (row stride ldx), the
+ * nn.Linear weights w_gate and w_up [n, k] (row strides ld_gate, ld_up), BF16 out [m, n] (row
+ * stride ldo); FP32 accumulation. 1 <= m <= 64 (the decode regime); k and the input row
+ * strides multiples of 8 with 16-byte aligned bases. block_m 16, 32 or 64 (0: the smallest
+ * >= m), block_k 64 or 128, num_stages the ring depth (0: 4), split_k the K ranges per weight
+ * (1, 2, 4; 0: automatic) -- a cluster of 2 x split_k CTAs shares each 128-column tile. */
+int hst_gated_mlp_stream(int32_t block_m, int32_t block_k, int32_t num_stages, int32_t split_k,
+                         const void* x, int64_t ldx, const void* w_gate, int64_t ld_gate,
+                         const void* w_up, int64_t ld_up, void* out, int64_t ldo, int64_t m,
+                         int64_t n, int64_t k, void* stream);
 
 /* Fused column-parallel GEMM (no reference counterpart). Rank `rank` of `world` (<= 9) holds
  * A [m, k] and its column slice B_r [k, n_total / world], both row-major contiguous. c_ranks[q]
