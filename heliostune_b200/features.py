@@ -11,10 +11,19 @@ onto the same six launch fields by :func:`launch_fields`:
 
 The v2 fields cannot tell the B200 families apart: a 256 x 256 pair tile, its split and stream-K
 forms and the 128-deep form differ in no field or in ``block_k`` alone, and a stream launch's
-split hides in ``group_m``. :func:`b200_joint_features` appends columns that name them: the
-family, the CTAs per cluster, the effective K splits and K per split, stream-K, the share of the
-B200's resident slots the launch keeps busy over its waves, and the family x log M products the
-crossovers between families follow.
+split hides in ``group_m``. :func:`b200_joint_features` appends two columns measured to help the
+cold-start bandit on B200 timing tables (``heliostune_b200.replay``):
+
+* ``log_roofline_tflops`` -- log2 of the throughput the shape's roofline allows on the B200
+  (the slower of 2MNK at the dense FP16 tensor peak and the FP16 operand bytes at the HBM
+  bandwidth, both as measured on this pool's B200s): the shape's baseline, the same for every
+  candidate, which a linear reward model otherwise has to assemble from the log M, N, K columns;
+* ``wave_fill`` -- the share of the B200's resident slots (SMs, CTA pairs or clusters of the
+  launch's size) the candidate's grid keeps busy over its waves; stream-K counts as full.
+
+Columns naming the family, cluster size, split count, K per split and stream-K were measured as
+well and made the replay worse (more parameters for the same probes), so they are not part of
+the basis; :func:`launch_shape` still describes each launch that way.
 """
 
 from __future__ import annotations
@@ -150,24 +159,15 @@ def v2_joint_features(
 
 
 #: The v2 columns followed by the B200 columns of :func:`b200_joint_features`.
-B200_FEATURE_NAMES: tuple[str, ...] = (
-    *V2_FEATURE_NAMES,
-    "family_persistent",
-    "family_split_k",
-    "family_stream",
-    "family_pair",
-    "cluster_ctas",
-    "k_splits",
-    "log_k_per_split",
-    "stream_k",
-    "wave_fill",
-    "stream_x_log_m",
-    "pair_x_log_m",
-    "split_k_x_log_m",
-)
+B200_FEATURE_NAMES: tuple[str, ...] = (*V2_FEATURE_NAMES, "log_roofline_tflops", "wave_fill")
+
+#: Dense FP16 tensor peak (TFLOP/s per 148 SMs) and HBM bandwidth (GB/s) measured on this pool's
+#: B200s (a cuBLAS GEMM and a device copy); they only set the scale of ``log_roofline_tflops``.
+B200_TENSOR_TFLOPS_PER_148_SMS = 1620.0
+B200_HBM_GBS = 6539.5
 
 
-class _Launch(NamedTuple):
+class LaunchShape(NamedTuple):
     family: str
     cluster: int  # CTAs per cluster (a CTA pair is 2)
     splits: int  # K intervals one output tile is summed from
@@ -176,7 +176,8 @@ class _Launch(NamedTuple):
     busy: float  # share of the resident slots busy over the launch's waves
 
 
-def _launch_shape(workload: Workload, config: object, sms: int) -> _Launch:
+def launch_shape(workload: Workload, config: object, sms: int) -> LaunchShape:
+    """How a candidate occupies the B200 for ``workload``: family, cluster, splits, busy share."""
     m, n, k = workload.m, workload.n, workload.k
     if isinstance(config, PairConfig):
         tiles = -(-m // 256) * -(-n // config.block_n)
@@ -184,18 +185,28 @@ def _launch_shape(workload: Workload, config: object, sms: int) -> _Launch:
         cluster = 2 * splits
         slots = resident_clusters(min(cluster, 8), sms)
         busy = 1.0 if config.split_k == PAIR_STREAM_K else wave_fill(tiles, slots)
-        return _Launch("pair", cluster, splits, config.block_k, config.split_k == PAIR_STREAM_K, busy)
+        return LaunchShape("pair", cluster, splits, config.block_k, config.split_k == PAIR_STREAM_K, busy)
     if isinstance(config, StreamConfig):
         splits = stream_splits(m, n, k, config, sms)
         ctas = -(-n // config.block_n)
-        return _Launch("stream", splits, splits, config.block_k, False, wave_fill(ctas, resident_clusters(splits, sms)))
+        return LaunchShape("stream", splits, splits, config.block_k, False, wave_fill(ctas, resident_clusters(splits, sms)))
     if isinstance(config, SplitKConfig):
         bk = 64 if config.block_k <= 64 else 128
         splits = split_plan(k, bk, config.split_k)[1]
-        return _Launch("split_k", 1, splits, bk, False, wave_fill(-(-n // config.block_n) * splits, sms))
-    tiles = -(-m // config.block_m) * -(-n // config.block_n)  # type: ignore[attr-defined]
+        return LaunchShape("split_k", 1, splits, bk, False, wave_fill(-(-n // config.block_n) * splits, sms))
+    if not isinstance(config, KernelConfig | HopperGemmConfig):
+        raise TypeError("unknown configuration type")
+    tiles = -(-m // config.block_m) * -(-n // config.block_n)
     family = "persistent" if isinstance(config, HopperGemmConfig) else "tile"
-    return _Launch(family, 1, 1, config.block_k, False, wave_fill(tiles, sms))  # type: ignore[attr-defined]
+    return LaunchShape(family, 1, 1, config.block_k, False, wave_fill(tiles, sms))
+
+
+def log_roofline_tflops(workload: Workload, sms: int) -> float:
+    """log2 of the roofline throughput (TFLOP/s) of ``workload`` on a B200 with ``sms`` SMs."""
+    flops = 2.0 * workload.m * workload.n * workload.k
+    nbytes = 2.0 * (workload.m * workload.k + workload.k * workload.n + workload.m * workload.n)
+    seconds = max(flops / (B200_TENSOR_TFLOPS_PER_148_SMS * sms / 148 * 1e12), nbytes / (B200_HBM_GBS * 1e9))
+    return math.log2(flops / seconds / 1e12)
 
 
 def b200_joint_features(
@@ -205,24 +216,6 @@ def b200_joint_features(
 ) -> NDArray[np.float64]:
     """The v2 vector of the same triple followed by the B200 columns (:data:`B200_FEATURE_NAMES`)."""
     fields = launch_fields(workload, config, hardware)
-    launch = _launch_shape(workload, config, hardware.multiprocessor_count)
-    log_m = math.log2(workload.m) / 14.0
-    is_stream = float(launch.family == "stream")
-    is_pair = float(launch.family == "pair")
-    is_split = float(launch.family == "split_k")
-    k_per_split = max(1.0, workload.k / launch.splits)
-    extra = (
-        float(launch.family == "persistent"),
-        is_split,
-        is_stream,
-        is_pair,
-        math.log2(launch.cluster) / 4.0,
-        math.log2(launch.splits) / 4.0,
-        math.log2(k_per_split) / 14.0,
-        float(launch.stream_k),
-        launch.busy,
-        is_stream * log_m,
-        is_pair * log_m,
-        is_split * log_m,
-    )
+    sms = hardware.multiprocessor_count
+    extra = (log_roofline_tflops(workload, sms) / 11.0, launch_shape(workload, config, sms).busy)
     return np.asarray((*_v2_values(workload, fields, hardware), *extra), dtype=np.float64)

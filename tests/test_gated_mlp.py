@@ -35,7 +35,7 @@ def _operands(m: int, k: int, n: int, seed: int) -> tuple[torch.Tensor, torch.Te
 
 
 def _reference(x: torch.Tensor, gate: torch.Tensor, up: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """The reference's FP32 result (before the BF16 rounding) and its BF16 output."""
+    """The reference's BF16 output (FP32 matmuls, TF32 off) and the exact value (FP64)."""
     previous = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
     try:
@@ -43,17 +43,21 @@ def _reference(x: torch.Tensor, gate: torch.Tensor, up: torch.Tensor) -> tuple[t
         u = torch.mm(x.float(), up.float().T)
     finally:
         torch.backends.cuda.matmul.allow_tf32 = previous
-    exact = torch.nn.functional.silu(g) * u
-    return exact, exact.to(torch.bfloat16)
+    expected = (torch.nn.functional.silu(g) * u).to(torch.bfloat16)
+    g64 = torch.mm(x.double(), gate.double().T)
+    exact = g64 * torch.sigmoid(g64) * torch.mm(x.double(), up.double().T)
+    return exact, expected
 
 
 def _check(out: torch.Tensor, x: torch.Tensor, gate: torch.Tensor, up: torch.Tensor) -> None:
     exact, expected = _reference(x, gate, up)
     assert out.shape == expected.shape and out.dtype == torch.bfloat16
     torch.testing.assert_close(out, expected, atol=0.02, rtol=0.02)  # the suite's policy
-    # within one BF16 ulp of the FP32 value (FP32 sums in another order, one rounding)
-    ulp = exact.abs() * 2.0**-7 + 1e-30
-    assert bool(((out.float() - exact).abs() <= ulp).all()), (out.float() - exact).abs().max().item()
+    # One BF16 ulp of the exact value, plus 1e-4 absolute: where the gate or up dot product
+    # cancels to ~1e-5 the FP32 accumulation over K (any order, cuBLAS's too) decides the bits.
+    bound = exact.abs() * 2.0**-7 + 1e-4
+    err = (out.double() - exact).abs()
+    assert bool((err <= bound).all()), (err - bound).max().item()
 
 
 @gpu
