@@ -93,7 +93,7 @@ def _config(args, workloads) -> dict[str, object]:
             "l2": "operands larger than L2",
         }
     workload = f"{args.workload}: {len(workloads)} shapes" if not args.shapes else f"shapes {args.shapes}"
-    selection = f"Thompson bandit, {args.budget} probes per shape on bank-1 tensors"
+    selection = f"Thompson bandit ({getattr(args, 'features', 'v2')} features), {args.budget} probes per shape on bank-1 tensors"
     if args.force:
         selection = f"forced: {args.force}"
     elif args.choices:
@@ -308,7 +308,9 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
 
         tuning = ProbeResult(probes={}, recommendations=dict(chosen))
     else:
-        tuning = thompson_probe(workloads, b200_candidates_for, measure, hardware, budget=args.budget, policy_seed=args.seed)
+        tuning = thompson_probe(
+            workloads, b200_candidates_for, measure, hardware, budget=args.budget, policy_seed=args.seed, basis=args.features
+        )
         for w in workloads:
             if w.key not in tuning.recommendations:
                 raise RuntimeError(f"no valid candidate for {w.key}")
@@ -1221,6 +1223,7 @@ def main() -> None:
     )
     parser.add_argument("--shapes", default=None, help="comma list of MxNxK overriding the workload")
     parser.add_argument("--budget", type=int, default=8, help="bandit probes per shape")
+    parser.add_argument("--features", choices=("v2", "b200"), default="v2", help="the bandit's feature basis")
     parser.add_argument("--probe-ms", type=float, default=10.0)
     parser.add_argument(
         "--confirm", type=int, default=3, help="re-time the best N probed candidates per shape in scored-like passes (1 = off)"

@@ -219,3 +219,7 @@ def b200_joint_features(
     sms = hardware.multiprocessor_count
     extra = (log_roofline_tflops(workload, sms) / 11.0, launch_shape(workload, config, sms).busy)
     return np.asarray((*_v2_values(workload, fields, hardware), *extra), dtype=np.float64)
+
+
+#: Feature bases by name: their column names and the function computing them.
+FEATURE_BASES = {"v2": (V2_FEATURE_NAMES, v2_joint_features), "b200": (B200_FEATURE_NAMES, b200_joint_features)}

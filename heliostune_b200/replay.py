@@ -51,7 +51,7 @@ from heliostune_b200.action_configs import (
 )
 from heliostune_b200.bandit import BayesianLinearBandit
 from heliostune_b200.configs import GRID_WORKLOADS, Workload
-from heliostune_b200.features import B200_FEATURE_NAMES, V2_FEATURE_NAMES, b200_joint_features, v2_joint_features
+from heliostune_b200.features import FEATURE_BASES
 from heliostune_b200.retrieval import log_tflops_reward
 from heliostune_b200.schema import HardwareProfile
 
@@ -65,10 +65,8 @@ PAIRED_SEED_STRIDE = 100_000
 REPLAY_PAIR_M_MINIMUM = 64
 
 FeatureFunction = Callable[[Workload, Any, HardwareProfile], np.ndarray]
-BASES: Mapping[str, tuple[tuple[str, ...], FeatureFunction]] = {
-    "v2": (V2_FEATURE_NAMES, v2_joint_features),
-    "b200": (B200_FEATURE_NAMES, b200_joint_features),
-}
+#: The bases compared by :func:`compare_feature_bases`.
+BASES: Mapping[str, tuple[tuple[str, ...], FeatureFunction]] = FEATURE_BASES
 
 
 def replay_candidates_for(workload: Workload) -> tuple[ActionCandidate, ...]:

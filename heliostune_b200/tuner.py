@@ -30,7 +30,7 @@ import numpy as np
 from heliostune_b200.action_configs import ActionCandidate
 from heliostune_b200.bandit import BayesianLinearBandit
 from heliostune_b200.configs import Workload
-from heliostune_b200.features import V2_FEATURE_NAMES, v2_joint_features
+from heliostune_b200.features import FEATURE_BASES
 from heliostune_b200.retrieval import log_tflops_reward
 from heliostune_b200.schema import HardwareProfile
 
@@ -90,15 +90,18 @@ def thompson_probe(
     noise_variance: float = NOISE_VARIANCE,
     prior_precision: float = PRIOR_PRECISION,
     model: BayesianLinearBandit | None = None,
+    basis: str = "v2",
 ) -> ProbeResult:
     """Probe ``budget`` candidates per workload with one shared Thompson-sampling posterior.
 
     ``measure`` returns the latency in milliseconds of one candidate on one workload and raises
-    to report a failure.
+    to report a failure. ``basis`` is the feature basis: the reference's ``"v2"`` or ``"b200"``
+    (v2 plus the shape's roofline throughput and the launch's wave fill).
     """
+    names, feature_fn = FEATURE_BASES[basis]
     if model is None:
         model = BayesianLinearBandit(
-            dimension=len(V2_FEATURE_NAMES),
+            dimension=len(names),
             noise_variance=noise_variance,
             prior_precision=prior_precision,
             seed=policy_seed,
@@ -111,7 +114,7 @@ def thompson_probe(
             available = tuple(c for c in candidates_for(workload) if c.key not in tried)
             if not available:
                 continue
-            features = partial(_features, workload, hardware)
+            features = partial(_features, feature_fn, workload, hardware)
             selected = model.choose(available, features)
             tried.add(selected.key)
             try:
@@ -128,5 +131,5 @@ def thompson_probe(
     return result
 
 
-def _features(workload: Workload, hardware: HardwareProfile, candidate: ActionCandidate) -> np.ndarray:
-    return v2_joint_features(workload, candidate.config, hardware)
+def _features(feature_fn, workload: Workload, hardware: HardwareProfile, candidate: ActionCandidate) -> np.ndarray:  # type: ignore[no-untyped-def]
+    return feature_fn(workload, candidate.config, hardware)
