@@ -11,7 +11,7 @@ family. This module restates that loop for B200 tables:
 
 * :func:`replay_candidates_for` -- the configurations a replay chooses among: every frozen
   candidate of the workload, the weight-streaming variants up to M = 256 and the CTA-pair
-  variants from M = 64 (plain, split, stream-K, 128-deep, 256 x 512, 256 x 128). About 14-21
+  variants from M = 64 (plain, split, stream-K, 128-deep, 256 x 512, 256 x 128). From 9 to 21
   per shape, more than the 8 probes, unlike the tuner's pool which holds at most 8.
 * :func:`collect_timing_table` (GPU) -- median latency of every such configuration on every
   workload in three banks of seeded operands, each launch after an L2 flush; a configuration
