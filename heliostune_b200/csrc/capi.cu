@@ -852,11 +852,19 @@ int launch_gated(const DeviceState& dev, const GatedProblem& p, int stages, int 
   using G = GatedShape<MP, BK>;
   static std::atomic<uint64_t> smem_done{0};
   HST_TRY(allow_smem(gated_stream_kernel<MP, BK>, smem_done));
+  const bool auto_stages = stages == 0;
+  if (auto_stages) stages = 4;
   if (stages < 2) stages = 2;
   if (stages > kStreamMaxStages) stages = kStreamMaxStages;
   if (splits == 0) splits = gated_auto_splits<MP, BK>(p.n, p.k, stages, dev.sm_count);
   int kb_per_split = 0, eff = 0;
   HST_TRY(split_plan(p.k, BK, splits, &kb_per_split, &eff));
+  if (auto_stages) {
+    // More CTAs than SMs: a shallower ring that lets two CTAs share an SM beats a second wave.
+    const int64_t ctas = cdiv(p.n, G::kNT) * 2 * eff;
+    while (ctas > dev.sm_count && stages > 3 && 2 * (G::smem_bytes(stages, 2 * eff) + kSmemReservedPerCta) > kSmemPerSm)
+      --stages;
+  }
   while (stages > 2 && G::smem_bytes(stages, 2 * eff) > kMaxDynamicSmem) --stages;
   if (G::smem_bytes(stages, 2 * eff) > kMaxDynamicSmem)
     return fail(HST_ERR_UNSUPPORTED, "gated tile does not fit shared memory");
@@ -1309,7 +1317,7 @@ int hst_gated_mlp_stream(int32_t block_m, int32_t block_k, int32_t num_stages, i
   DeviceState* dev = nullptr;
   HST_TRY(device_state(&dev));
   const GatedProblem p{x, ldx, w_gate, ld_gate, w_up, ld_up, out, ldo, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k)};
-  const int stages = num_stages == 0 ? 4 : num_stages;
+  const int stages = num_stages;  // 0: automatic
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 #define HST_GATED_CASE(MP_, BK_) \
   if (block_m == MP_ && block_k == BK_) return launch_gated<MP_, BK_>(*dev, p, stages, split_k, s);

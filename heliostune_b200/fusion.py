@@ -317,3 +317,51 @@ def load_rmsnorm(entrypoint: str) -> Callable[..., torch.Tensor]:
     if entrypoint not in RMSNORM_ENTRYPOINTS:
         raise KeyError(f"unknown RMSNorm entry point {entrypoint!r}")
     return rmsnorm
+
+
+def _main(argv: list[str] | None = None) -> None:
+    """``python -m heliostune_b200.fusion {gated,residual} [--batch B] [--reps R]``: runs one op on
+    seeded inputs of the reference's suite shapes (gated: x [B, 4096], weights [11008, 4096];
+    residual: 128 x 4096) and prints the median event time of R launches, each after an L2
+    flush. Meant for profiling a single kernel."""
+    import argparse
+    import json
+
+    from heliostune_b200.timing import flush_buffer
+
+    parser = argparse.ArgumentParser(description=_main.__doc__.split("\n")[0])
+    parser.add_argument("op", choices=("gated", "residual"))
+    parser.add_argument("--batch", type=int, default=8)
+    parser.add_argument("--reps", type=int, default=3)
+    args = parser.parse_args(argv)
+    device = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=device).manual_seed(17)
+    if args.op == "gated":
+        x = torch.randn((args.batch, 4096), generator=g, device=device).to(torch.bfloat16)
+        gate = (torch.randn((11008, 4096), generator=g, device=device) / 64).to(torch.bfloat16)
+        up = (torch.randn((11008, 4096), generator=g, device=device) / 64).to(torch.bfloat16)
+
+        def run() -> torch.Tensor:
+            return gated_mlp(x, gate, up)
+    else:
+        x = torch.randn(RESIDUAL_RMSNORM_SHAPE, generator=g, device=device).to(torch.bfloat16)
+        r = torch.randn(RESIDUAL_RMSNORM_SHAPE, generator=g, device=device).to(torch.bfloat16)
+        gamma = (1 + 0.02 * torch.randn((RESIDUAL_RMSNORM_SHAPE[1],), generator=g, device=device)).to(torch.bfloat16)
+
+        def run() -> torch.Tensor:
+            return residual_rmsnorm_w8(x, r, gamma)
+    flush = flush_buffer(device)
+    times = []
+    for _ in range(args.reps):
+        flush.zero_()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        run()
+        end.record()
+        torch.cuda.synchronize(device)
+        times.append(start.elapsed_time(end) * 1e3)
+    print(json.dumps({"op": args.op, "batch": args.batch, "us": sorted(times)[len(times) // 2]}))
+
+
+if __name__ == "__main__":
+    _main()

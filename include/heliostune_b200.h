@@ -170,7 +170,8 @@ int hst_residual_rmsnorm(const void* x, int64_t ldx, const void* residual, int64
  * nn.Linear weights w_gate and w_up [n, k] (row strides ld_gate, ld_up), BF16 out [m, n] (row
  * stride ldo); FP32 accumulation. 1 <= m <= 64 (the decode regime); k and the input row
  * strides multiples of 8 with 16-byte aligned bases. block_m 16, 32 or 64 (0: the smallest
- * >= m), block_k 64 or 128, num_stages the ring depth (0: 4), split_k the K ranges per weight
+ * >= m), block_k 64 or 128, num_stages the ring depth (0: 4, or 3 where that lets two CTAs
+ * share an SM because the grid holds more CTAs than SMs), split_k the K ranges per weight
  * (1, 2, 4; 0: automatic) -- a cluster of 2 x split_k CTAs shares each 128-column tile. */
 int hst_gated_mlp_stream(int32_t block_m, int32_t block_k, int32_t num_stages, int32_t split_k,
                          const void* x, int64_t ldx, const void* w_gate, int64_t ld_gate,
