@@ -46,6 +46,8 @@ def test_metric_name_is_baselines_for_the_grid_only() -> None:
     assert "28-shape FP16 sweep" in bench._metric(sweep, 28)
     custom = argparse.Namespace(workload="grid", shapes="512x4608x3584")
     assert "1-shape FP16 custom shapes" in bench._metric(custom, 1)
+    colpar = argparse.Namespace(workload="colpar", shapes=None)
+    assert bench._metric(colpar, 1) == bench.COLPAR_METRIC  # both arms print this name
 
 
 def test_kernel_families() -> None:
