@@ -290,6 +290,14 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
             raise ValueError(f"parity failure (normwise {err:.3g})")
         return do_bench(lambda: launch(a, b, candidate), warmup_ms=2.0, rep_ms=args.probe_ms, quantiles=(0.5,))[0]
 
+    # ---- 0. the pre-timing correctness gate: every pool candidate on a small sample --------
+    from heliostune_b200.configs import validation_workloads
+    from heliostune_b200.hopper_kernel import assert_candidate_kernels_correct
+
+    gate = assert_candidate_kernels_correct(
+        "B200", candidates_for=b200_candidates_for, workloads=validation_workloads(workloads)
+    )
+
     t0 = time.perf_counter()
     chosen = {}
     if args.force:
@@ -508,6 +516,7 @@ def run_ours(args: argparse.Namespace) -> dict[str, object] | None:
         "data": "synthetic: seeded N(0,1)/sqrt(K) FP16 operands",
         "config": _config(args, workloads),
         "confirm_changed_shapes": confirmed,
+        "pre_timing_gate": f"{len(gate)} candidate checks on {len(validation_workloads(workloads))} sampled shapes, all correct",
         "parity": parity,
         "geomean_latency_vs_cublas": round(geomean, 4),
         "cublas_tflops": round(total_flops / (sum(cublas_ms) / 1e3) / 1e12, 3),

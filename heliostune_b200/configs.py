@@ -266,6 +266,34 @@ EDGE_WORKLOADS: tuple[Workload, ...] = (
 )
 
 
+def validation_workloads(
+    workloads: tuple[Workload, ...] | list[Workload] = DEFAULT_WORKLOADS,
+    *,
+    edges: tuple[Workload, ...] | list[Workload] = EDGE_WORKLOADS,
+) -> tuple[Workload, ...]:
+    """The pre-timing gate's sample (``hopper_spec.py:26-55``): per token regime the workloads with
+    the smallest and the largest N x K, then the edge shapes, each once, in that order."""
+    from heliostune_b200.errors import ProtocolError
+
+    if not workloads:
+        raise ProtocolError("validation workload manifest must not be empty")
+    regimes: dict[str, list[Workload]] = {}
+    for workload in workloads:
+        if type(workload) is not Workload:
+            raise ProtocolError("validation workload manifest must contain only Workload values")
+        regimes.setdefault(workload.regime, []).append(workload)
+    chosen: dict[str, Workload] = {}
+    for regime in sorted(regimes):
+        by_size = sorted(regimes[regime], key=lambda w: (w.n * w.k, w.key))
+        chosen.setdefault(by_size[0].key, by_size[0])
+        chosen.setdefault(by_size[-1].key, by_size[-1])
+    for workload in edges:
+        if type(workload) is not Workload:
+            raise ProtocolError("validation edge manifest must contain only Workload values")
+        chosen.setdefault(workload.key, workload)
+    return tuple(chosen.values())
+
+
 # --------------------------------------------------------------------------------------------
 # The measurement grids of this build (Llama-3-8B and Qwen2.5-7B projections).
 # --------------------------------------------------------------------------------------------

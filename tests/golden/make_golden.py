@@ -358,6 +358,13 @@ def collection_fixtures(root: Path) -> None:
     )
 
 
+def validation_fixtures() -> None:
+    """The reference's pre-timing gate sample (hopper_spec.py:26-55) over its 96 workloads."""
+    from heliostune.hopper_spec import validation_workloads
+
+    _dump("validation_workloads.json", {"keys": [w.key for w in validation_workloads()]})
+
+
 def main() -> None:
     if len(sys.argv) != 2:
         raise SystemExit("usage: python tests/golden/make_golden.py <path of the reference checkout>")
@@ -370,6 +377,7 @@ def main() -> None:
     gemm_fixtures()
     rmsnorm_fixtures()
     collection_fixtures(root)
+    validation_fixtures()
 
 
 if __name__ == "__main__":

@@ -300,3 +300,18 @@ def test_deep_k_and_narrow_pair_candidates() -> None:
         PairConfig(256, 512, 128, 4, 4, 8)
     with pytest.raises(SchemaError):
         PairConfig(256, 512, 64, 4, 4, 8, 2)
+
+
+def test_validation_sample_is_the_reference_gate_sample() -> None:
+    """The pre-timing gate's workload sample equals the one the reference's own
+    ``validation_workloads`` picks (tests/golden/validation_workloads.json)."""
+    from heliostune_b200.configs import EDGE_WORKLOADS, GRID_WORKLOADS, validation_workloads
+    from heliostune_b200.errors import ProtocolError
+    from tests.conftest import load_golden
+
+    assert [w.key for w in validation_workloads()] == load_golden("validation_workloads.json")["keys"]
+    grid = validation_workloads(GRID_WORKLOADS)
+    assert len(grid) == 2 * 12 + len(EDGE_WORKLOADS)
+    assert {w.m for w in grid} >= {1, 8192}
+    with pytest.raises(ProtocolError):
+        validation_workloads(())

@@ -388,3 +388,33 @@ def test_empty_and_degenerate_extents() -> None:
     assert out.shape == (5, 16) and bool((out == 0).all())
     with pytest.raises(ValueError, match="split-K requires"):
         launch(torch.zeros((32, 64), device="cuda", dtype=torch.float16), torch.zeros((64, 16), device="cuda", dtype=torch.float16), SPLIT_K_CANDIDATES[0])
+
+
+def test_pre_timing_gate_passes_every_family_and_journals_failures(monkeypatch: pytest.MonkeyPatch) -> None:
+    """The reference's gate (hopper_kernel.py:498-623) over every family of this library on the
+    edge shapes; a wrong kernel is a journal entry, and the asserting form raises on it."""
+    from heliostune_b200 import action_expansion
+    from heliostune_b200.action_configs import pair_candidates_for, stream_candidates_for
+    from heliostune_b200.errors import ProtocolError
+    from heliostune_b200.hopper_kernel import assert_candidate_kernels_correct, validate_candidate_kernels
+
+    def every_family(w: Workload) -> tuple[ActionCandidate, ...]:
+        frozen = tuple(c for c in ALL_CANDIDATES if c.family != "split_k" or w.m <= 31)
+        pairs = (*PAIR_CANDIDATES, PAIR_DEEP_K, PAIR_NARROW) if w.m > 128 else ()
+        return (*frozen, *stream_candidates_for(w), *pairs)
+
+    results = assert_candidate_kernels_correct("B200", candidates_for=every_family, workloads=EDGE_WORKLOADS)
+    assert len(results) == sum(len(every_family(w)) for w in EDGE_WORKLOADS)
+    assert {r.kernel for r in results} == {"tile", "persistent", "split_k", "stream", "pair"}
+    real = action_expansion.launch
+
+    def wrong_pair(a, b, candidate):  # type: ignore[no-untyped-def]
+        out = real(a, b, candidate)
+        return out + 1 if candidate.family == "pair" else out
+
+    monkeypatch.setattr(action_expansion, "launch", wrong_pair)
+    journal = validate_candidate_kernels(candidates_for=every_family, workloads=EDGE_WORKLOADS)
+    assert {r.kernel for r in journal if not r.correct} == {"pair"}
+    assert all(r.error and "correctness check failed" in r.error for r in journal if not r.correct)
+    with pytest.raises(ProtocolError, match="candidate kernel checks failed"):
+        assert_candidate_kernels_correct(candidates_for=every_family, workloads=EDGE_WORKLOADS)
