@@ -670,13 +670,16 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
 
         fused = FusedColumnParallel(w.m, w.n, device=device)
 
-        def step(events):
-            return fused(a, b_shard, phase_events=events)
+        def step_on(x, y, events):
+            return fused(x, y, phase_events=events)
     else:
         fused = None
 
-        def step(events):
-            return column_parallel_matmul(a, b_shard, phase_events=events)
+        def step_on(x, y, events):
+            return column_parallel_matmul(x, y, phase_events=events)
+
+    def step(events):
+        return step_on(a, b_shard, events)
 
     for _ in range(args.warmup):
         step(None)
@@ -712,14 +715,15 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
 
     parity = _colpar_parity(w, a, out, world, shard.cols, device)
     del out
-    times = torch.tensor([step_ms, gemm_ms, phase1_ms, phase2_ms], device=device, dtype=torch.float64)
+    e2e_ms = _colpar_e2e(a, b_shard, shard, step_on, device, args.e2e_steps) if args.e2e_steps > 0 else step_ms
+    times = torch.tensor([step_ms, gemm_ms, phase1_ms, phase2_ms, e2e_ms], device=device, dtype=torch.float64)
     checks = torch.tensor(
         [parity["normwise"], parity["normwise_cublas"], 0.0 if parity["ok"] else 1.0], device=device, dtype=torch.float64
     )
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
         dist.all_reduce(checks, op=dist.ReduceOp.MAX)
-    step_ms, gemm_ms, phase1_ms, phase2_ms = (float(t) for t in times.tolist())
+    step_ms, gemm_ms, phase1_ms, phase2_ms, e2e_ms = (float(t) for t in times.tolist())
     normwise, normwise_cublas, failed = (float(t) for t in checks.tolist())
     peaks, source = _peaks()
     flops = 2.0 * w.m * w.n * w.k
@@ -767,6 +771,17 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
         "step_roofline_frac": round(t_roof / (step_ms / 1e3), 4),
         "step_roofline_limiter": limiter,
         "exchange_bytes_per_gpu": int(gather_bytes),
+        "e2e": {
+            "value": round(flops / (e2e_ms / 1e3) / 1e12, 3),
+            "unit": "TFLOP/s",
+            "h2d_bytes_per_step": world * 2 * (w.m * w.k + w.k * shard.cols),
+            "d2h_bytes_per_step": 2 * w.m * w.n,
+            "note": (
+                "one step with host buffers: every rank copies A and its B slice in from pinned memory, runs "
+                "the step, and copies its own column slice of C out (the ranks return all of C once); bytes are "
+                "the whole job's; time from the first copy to the last, max over ranks"
+            ),
+        },
         "gpu_launches": (1 if fused is not None or world == 1 else 2) * args.steps,
         "clocks": sampler.summary(epoch0, epoch1),
         "status_bits": _native.status(local_rank),
@@ -792,6 +807,32 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
         print(json.dumps(result), flush=True) if rank == 0 else None
         raise SystemExit("column-parallel parity failure")
     return result if rank == 0 else None
+
+
+def _colpar_e2e(a, b_shard, shard, step_on, device, steps: int) -> float:
+    """Milliseconds of one config-5 step with host buffers on this rank (the slowest rank's is
+    the job's): H2D of A and of this rank's B slice from pinned memory into device buffers
+    allocated beforehand, the step (GEMM and exchange), D2H of this rank's column slice of C into
+    pinned memory; the first of ``steps + 1`` passes warms up."""
+    import torch
+
+    a_host, b_host = a.cpu().pin_memory(), b_shard.cpu().pin_memory()
+    a_dev, b_dev = torch.empty_like(a), torch.empty_like(b_shard)
+    c_host = torch.empty((a.shape[0], shard.cols), dtype=torch.float16).pin_memory()
+    total = 0.0
+    for rep in range(steps + 1):
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        a_dev.copy_(a_host, non_blocking=True)
+        b_dev.copy_(b_host, non_blocking=True)
+        c = step_on(a_dev, b_dev, None)
+        c_host.copy_(c[:, shard.start : shard.stop], non_blocking=True)
+        end.record()
+        torch.cuda.synchronize(device)
+        if rep > 0:
+            total += start.elapsed_time(end) / steps
+    return total
 
 
 def _colpar_a(w, device):
