@@ -80,27 +80,18 @@ def _config(args, workloads) -> dict[str, object]:
     """The ``config`` object of the JSON line; both arms print the same one."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.workload == "colpar":
-        from heliostune_b200.column_parallel import column_parallel_candidate, exchange_candidate
+        from heliostune_b200.column_parallel import column_parallel_candidate
 
         (w,) = workloads
-        descriptions = {
-            "fused": "fused: GEMM epilogue stores every tile to all ranks over NVLink",
-            "copies": "copy engines: each finished row band of the slice copied to all ranks while the GEMM runs",
-        }
         exchange = (
-            descriptions[args.exchange]
-            if args.exchange in descriptions and world > 1
+            "fused: GEMM epilogue stores every tile to all ranks over NVLink"
+            if args.exchange == "fused" and world > 1
             else "NCCL all-gather + column assembly" if world > 1 else "none (one rank holds all of N)"
-        )
-        gemm = (
-            exchange_candidate(w.m, w.n // world, world, "copies", getattr(args, "band_rows", None))
-            if args.exchange == "copies" and world > 1
-            else column_parallel_candidate(w.m, w.n // world)
         )
         return {
             "workload": f"colpar M={w.m} N={w.n} K={w.k}",
             "parallelism": f"column-parallel x{world}",
-            "gemm": gemm.key,
+            "gemm": column_parallel_candidate(w.m, w.n // world).key,
             "exchange": exchange,
             "l2": "operands larger than L2",
         }
@@ -674,17 +665,10 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
     b_shard = _colpar_b_slice(w, shard.cols, rank, device)
     candidate = column_parallel_candidate(w.m, shard.cols)
 
-    if args.exchange in ("fused", "copies") and world > 1:
+    if args.exchange == "fused" and world > 1:
         from heliostune_b200.column_parallel import FusedColumnParallel
 
-        fused = FusedColumnParallel(
-            w.m,
-            w.n,
-            device=device,
-            exchange="stores" if args.exchange == "fused" else "copies",
-            band_rows=args.band_rows,
-        )
-        candidate = fused.candidate  # the copy-engine form rasters in its bands
+        fused = FusedColumnParallel(w.m, w.n, device=device)
 
         def step_on(x, y, events):
             return fused(x, y, phase_events=events)
@@ -798,15 +782,13 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
                 "the whole job's; time from the first copy to the last, max over ranks"
             ),
         },
-        # Per step: the fused GEMM; the band GEMM and its release kernel; or the GEMM and the assembly.
-        "gpu_launches": (1 if (fused is not None and args.exchange == "fused") or world == 1 else 2) * args.steps,
+        "gpu_launches": (1 if fused is not None or world == 1 else 2) * args.steps,
         "clocks": sampler.summary(epoch0, epoch1),
         "status_bits": _native.status(local_rank),
     }
     if world > 1:
         if fused is not None:
-            first = "barrier+fused_gemm" if args.exchange == "fused" else "barrier+gemm+band_copies"
-            result["phases_ms"] = {first: round(phase1_ms, 4), "trailing_barrier": round(phase2_ms, 4)}
+            result["phases_ms"] = {"barrier+fused_gemm": round(phase1_ms, 4), "trailing_barrier": round(phase2_ms, 4)}
             result["exchange_gbs"] = round(gather_bytes / (step_ms / 1e3) / 1e9, 1)
             result["exchange_gbs_note"] = "bytes each GPU receives / step time (the exchange overlaps the GEMM)"
         else:
@@ -1347,22 +1329,11 @@ def main() -> None:
     parser.add_argument("--force", default=None, help="profiling runs: one candidate key for every shape")
     parser.add_argument(
         "--exchange",
-        choices=("fused", "copies", "nccl"),
+        choices=("fused", "nccl"),
         default="fused",
-        help=(
-            "colpar: all-gather fused into the GEMM epilogue, row bands copied by the copy engines while "
-            "the GEMM runs, or NCCL all-gather + assembly"
-        ),
-    )
-    parser.add_argument(
-        "--band-rows",
-        type=int,
-        default=None,
-        help="colpar --exchange copies: tile rows (256 rows of C) per copied band (default: 2 at 8 GPUs, else 4)",
+        help="colpar: all-gather fused into the GEMM epilogue, or NCCL all-gather + assembly",
     )
     args = parser.parse_args()
-    if args.band_rows is not None and args.band_rows < 1:
-        parser.error("--band-rows must be >= 1")
     if args.workload is None:
         args.workload = "colpar" if _distributed_launch() and not args.shapes else "grid"
     if args.warmup < 3 and args.impl == "ours" and not args.shapes:

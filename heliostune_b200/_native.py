@@ -62,7 +62,6 @@ EXPORTED_SYMBOLS = (
     "hst_matmul_split_k_noalloc",
     "hst_column_assemble",
     "hst_matmul_pair_fanout",
-    "hst_matmul_pair_band_copies",
     "hst_ipc_export",
     "hst_ipc_import",
     "hst_ipc_close",
@@ -172,12 +171,6 @@ def _declare(lib: ctypes.CDLL) -> None:
         "hst_ipc_close": ([_ptr], ctypes.c_int),
         "hst_matmul_pair_fanout": (
             [_i32] * 4 + [_ptr, _ptr, ctypes.POINTER(ctypes.c_void_p), _i32, _i32, _i64, _i64, _i64, _ptr],
-            ctypes.c_int,
-        ),
-        "hst_matmul_pair_band_copies": (
-            [_i32] * 4
-            + [_ptr, _ptr, ctypes.POINTER(ctypes.c_void_p), _i32, _i32, _i64, _i64, _i64]
-            + [_ptr, _i64, ctypes.c_uint32, ctypes.POINTER(ctypes.c_void_p), _ptr],
             ctypes.c_int,
         ),
         "hst_matmul_split_k_noalloc": (

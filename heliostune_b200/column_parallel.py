@@ -10,7 +10,6 @@ local memory; no TMA load in this library reads another GPU's memory or feeds se
 
 from __future__ import annotations
 
-import dataclasses
 from collections.abc import Callable
 from dataclasses import dataclass
 
@@ -96,45 +95,16 @@ def assemble_columns(gathered: torch.Tensor, out: torch.Tensor | None = None) ->
     return out
 
 
-#: The exchange forms of :class:`FusedColumnParallel`.
-EXCHANGES = ("stores", "copies")
-
-
-def band_tile_rows(world: int) -> int:
-    """Tile rows (of 256 rows of C) per band in the copy-engine exchange: small bands where the
-    exchange bounds the step (8 GPUs), so the copies start early and the last band's transfer
-    after the GEMM is short; larger ones below, where the GEMM's raster locality matters more."""
-    return 2 if world >= 8 else 4
-
-
-def exchange_candidate(m: int, cols: int, world: int, exchange: str, band_rows: int | None = None) -> ActionCandidate:
-    """The slice GEMM a :class:`FusedColumnParallel` of this exchange runs: the copy-engine form
-    rasters in bands of ``band_rows`` tile rows (:func:`band_tile_rows` by default)."""
-    candidate = column_parallel_candidate(m, cols)
-    if exchange == "copies":
-        rows = band_tile_rows(world) if band_rows is None else band_rows
-        candidate = ActionCandidate(dataclasses.replace(candidate.config, group_m=rows))
-    return candidate
-
-
 class FusedColumnParallel:
-    """Column-parallel GEMM whose all-gather overlaps the GEMM.
+    """Column-parallel GEMM whose all-gather is fused into the GEMM epilogue.
 
     Every rank allocates its full output ``C [M, N]`` once (``torch.empty``), exports its CUDA
     IPC handle, and maps every peer's output (``hst_ipc_*``). A call runs the persistent CTA-pair
-    GEMM on this rank's column slice, with one of two exchanges:
-
-    * ``"stores"``: each finished sub-tile goes to the local C by TMA and to every peer's C by
-      coalesced NVLink stores from the epilogue while the next tiles compute
-      (``hst_matmul_pair_fanout``);
-    * ``"copies"``: the GEMM writes the local C only and counts finished tiles per band of
-      ``band_rows`` tile rows; ``world - 1`` copy streams wait for each band (stream memory
-      waits) and copy it into the peers' C on the copy engines while the GEMM runs on
-      (``hst_matmul_pair_band_copies``), leaving the SMs to the GEMM.
-
-    NCCL barriers before and after the launch order the ranks: no peer writes into a C that is
-    still being read, and C is complete when the call returns. The returned tensor is this
-    object's buffer and is overwritten by the next call.
+    GEMM on this rank's column slice; each finished sub-tile goes to the local C by TMA and to
+    every peer's C by coalesced NVLink stores while the next tiles compute
+    (``hst_matmul_pair_fanout``). NCCL barriers before and after the launch order the ranks: no
+    peer writes into a C that is still being read, and C is complete when the call returns.
+    The returned tensor is this object's buffer and is overwritten by the next call.
     """
 
     def __init__(
@@ -145,35 +115,21 @@ class FusedColumnParallel:
         group: dist.ProcessGroup | None = None,
         candidate: ActionCandidate | None = None,
         device: torch.device | None = None,
-        exchange: str = "stores",
-        band_rows: int | None = None,
     ) -> None:
         import ctypes
 
-        if exchange not in EXCHANGES:
-            raise ValueError(f"exchange must be one of {EXCHANGES}, not {exchange!r}")
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.shard = ColumnShard(n_total, self.world, self.rank)
         if candidate is None:
-            candidate = exchange_candidate(m, self.shard.cols, self.world, exchange, band_rows)
-        elif exchange == "copies" and band_rows is not None:
-            candidate = ActionCandidate(dataclasses.replace(candidate.config, group_m=band_rows))
-        if not isinstance(candidate.config, PairConfig) or candidate.config.split_k != 1:
-            raise ValueError("the fused column-parallel GEMM runs the persistent CTA-pair kernel")
-        self.exchange = exchange
-        self.candidate = candidate  # in the copy-engine form its raster group is the band
+            candidate = column_parallel_candidate(m, self.shard.cols)
+        if not isinstance(candidate.config, PairConfig):
+            raise ValueError("the fused column-parallel GEMM runs the CTA-pair kernel")
+        self.candidate = candidate
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.out = torch.empty((m, n_total), dtype=torch.float16, device=self.device)
         self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
-        self.bands = -(-(-(-m // 256)) // candidate.config.group_m)
-        self._band_words = torch.zeros(self.bands, dtype=torch.int32, device=self.device)
-        self._epoch = 0
-        self._copy_streams = [torch.cuda.Stream(self.device) for _ in range(self.world - 1)] if exchange == "copies" else []
-        self._copy_handles = (ctypes.c_void_p * max(1, len(self._copy_streams)))(
-            *[st.cuda_stream for st in self._copy_streams]
-        )
         lib = _native.library()
         handle = (ctypes.c_char * 64)()
         offset = ctypes.c_uint64(0)
@@ -215,53 +171,23 @@ class FusedColumnParallel:
         if phase_events:
             phase_events[0].record()
         self._barrier()  # every rank is done reading the previous result
-        lib = _native.library()
-        if self.exchange == "stores":
-            _native.check(
-                lib.hst_matmul_pair_fanout(
-                    config.block_n,
-                    config.block_k,
-                    config.num_stages,
-                    config.group_m,
-                    a.data_ptr(),
-                    b_shard.data_ptr(),
-                    self._pointers,
-                    self.world,
-                    self.rank,
-                    m,
-                    self.shard.n_total,
-                    k,
-                    _stream(self.device),
-                )
+        _native.check(
+            _native.library().hst_matmul_pair_fanout(
+                config.block_n,
+                config.block_k,
+                config.num_stages,
+                config.group_m,
+                a.data_ptr(),
+                b_shard.data_ptr(),
+                self._pointers,
+                self.world,
+                self.rank,
+                m,
+                self.shard.n_total,
+                k,
+                _stream(self.device),
             )
-        else:
-            main = torch.cuda.current_stream(self.device)
-            for st in self._copy_streams:
-                st.wait_stream(main)  # the copies start after the barrier above
-            self._epoch = self._epoch % 0xFFFFFFFF + 1
-            _native.check(
-                lib.hst_matmul_pair_band_copies(
-                    config.block_n,
-                    config.block_k,
-                    config.num_stages,
-                    config.group_m,
-                    a.data_ptr(),
-                    b_shard.data_ptr(),
-                    self._pointers,
-                    self.world,
-                    self.rank,
-                    m,
-                    self.shard.n_total,
-                    k,
-                    self._band_words.data_ptr(),
-                    self.bands,
-                    self._epoch,
-                    self._copy_handles,
-                    main.cuda_stream,
-                )
-            )
-            for st in self._copy_streams:
-                main.wait_stream(st)  # every band has reached every peer
+        )
         if phase_events:
             phase_events[1].record()
         self._barrier()  # every rank's slices have landed everywhere

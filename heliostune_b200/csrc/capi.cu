@@ -1019,81 +1019,6 @@ int gemm_impl(const hst_gemm_config* cfg, const void* a, int64_t sa0, int64_t sa
                   static_cast<uint8_t*>(workspace), nullptr, stream);
 }
 
-// One rank's launch of a column-parallel GEMM: the pair plan for its [m, n_total / world] slice
-// and the operands, with C this rank's columns of its own full output.
-struct ColumnLaunch {
-  DeviceState* dev = nullptr;
-  Plan plan;
-  Operands o;
-  int64_t cols = 0;
-};
-
-int prepare_column_launch(int32_t block_n, int32_t block_k, int32_t num_stages, int32_t group_m,
-                          const void* a, const void* b_slice, void* const* c_ranks, int32_t world,
-                          int32_t rank, int64_t m, int64_t n_total, int64_t k, ColumnLaunch* out) {
-  if (world < 1 || world > kMaxPeers + 1 || rank < 0 || rank >= world)
-    return fail(HST_ERR_INVALID, "world %d / rank %d out of range (at most %d ranks)", world, rank,
-                kMaxPeers + 1);
-  if (n_total % world != 0) return fail(HST_ERR_INVALID, "N must split evenly over the ranks");
-  const int64_t cols = n_total / world;
-  if (cols % 8 != 0 || k % 8 != 0)
-    return fail(HST_ERR_INVALID, "the column slice and K must be multiples of 8");
-  if (c_ranks == nullptr || a == nullptr || b_slice == nullptr)
-    return fail(HST_ERR_INVALID, "null pointer");
-  for (int q = 0; q < world; ++q)
-    if (c_ranks[q] == nullptr) return fail(HST_ERR_INVALID, "null output of rank %d", q);
-  HST_TRY(check_problem(a, b_slice, c_ranks[rank], m, cols, k, n_total));
-  HST_TRY(device_state(&out->dev));
-  const hst_gemm_config cfg{HST_FAMILY_PAIR, 256, block_n, block_k, 4, num_stages, group_m, 1};
-  const View va{static_cast<const __half*>(a), m, k, k, 1};
-  const View vb{static_cast<const __half*>(b_slice), k, cols, cols, 1};
-  HST_TRY(make_plan(&cfg, va, vb, m, cols, k, out->dev->sm_count, &out->plan));
-  if (out->plan.pack_a || out->plan.pack_b)
-    return fail(HST_ERR_INVALID, "operands must be 16-byte aligned row-major");
-  Operands& o = out->o;
-  o.m = static_cast<int>(m);
-  o.n = static_cast<int>(cols);
-  o.k = static_cast<int>(k);
-  o.a = va.ptr;
-  o.lda = k;
-  o.b = vb.ptr;
-  o.ldb = cols;
-  o.c = static_cast<__half*>(c_ranks[rank]) + rank * cols;
-  o.ldc = n_total;
-  if ((reinterpret_cast<uintptr_t>(o.c) & 15) != 0 || n_total % 8 != 0)
-    return fail(HST_ERR_INVALID, "output rows must be 16-byte aligned");
-  out->cols = cols;
-  return HST_OK;
-}
-
-int launch_column_pair(const ColumnLaunch& l, const PairFanoutArgs& fanout, cudaStream_t s) {
-  const Plan& p = l.plan;
-  if (p.bn == 256 && p.bk == 64) return launch_pair<256, 64, false>(*l.dev, l.o, p.stages, p.group_m, 1, 0, s, &fanout);
-  if (p.bn == 128 && p.bk == 64) return launch_pair<128, 64, false>(*l.dev, l.o, p.stages, p.group_m, 1, 0, s, &fanout);
-  if (p.bn == 256 && p.bk == 128) return launch_pair<256, 128, false>(*l.dev, l.o, p.stages, p.group_m, 1, 0, s, &fanout);
-  if (p.bn == 128 && p.bk == 128) return launch_pair<128, 128, false>(*l.dev, l.o, p.stages, p.group_m, 1, 0, s, &fanout);
-  if (p.bn == 512 && p.bk == 64) return launch_pair<512, 64, false>(*l.dev, l.o, p.stages, p.group_m, 1, 0, s, &fanout);
-  return fail(HST_ERR_UNSUPPORTED, "no pair kernel for N %d, K %d", p.bn, p.bk);
-}
-
-// cuStreamWaitValue32, from the driver through the runtime's entry-point query.
-typedef CUresult (*PfnStreamWaitValue32)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
-int stream_wait_value_fn(PfnStreamWaitValue32* out) {
-  static std::atomic<PfnStreamWaitValue32> fn{nullptr};
-  PfnStreamWaitValue32 f = fn.load(std::memory_order_acquire);
-  if (f == nullptr) {
-    cudaDriverEntryPointQueryResult q;
-    void* raw = nullptr;
-    HST_CUDA(cudaGetDriverEntryPointByVersion("cuStreamWaitValue32", &raw, 12000, cudaEnableDefault, &q));
-    if (q != cudaDriverEntryPointSuccess || raw == nullptr)
-      return fail(HST_ERR_CUDA, "cuStreamWaitValue32 unavailable");
-    f = reinterpret_cast<PfnStreamWaitValue32>(raw);
-    fn.store(f, std::memory_order_release);
-  }
-  *out = f;
-  return HST_OK;
-}
-
 }  // namespace
 }  // namespace hst
 
@@ -1240,72 +1165,52 @@ int hst_matmul_pair(int32_t block_n, int32_t block_k, int32_t num_stages, int32_
 int hst_matmul_pair_fanout(int32_t block_n, int32_t block_k, int32_t num_stages, int32_t group_m,
                            const void* a, const void* b_slice, void* const* c_ranks, int32_t world,
                            int32_t rank, int64_t m, int64_t n_total, int64_t k, void* stream) {
-  ColumnLaunch l;
-  HST_TRY(prepare_column_launch(block_n, block_k, num_stages, group_m, a, b_slice, c_ranks, world,
-                                rank, m, n_total, k, &l));
+  if (world < 1 || world > kMaxPeers + 1 || rank < 0 || rank >= world)
+    return fail(HST_ERR_INVALID, "world %d / rank %d out of range (at most %d ranks)", world, rank,
+                kMaxPeers + 1);
+  if (n_total % world != 0) return fail(HST_ERR_INVALID, "N must split evenly over the ranks");
+  const int64_t cols = n_total / world;
+  if (cols % 8 != 0 || k % 8 != 0)
+    return fail(HST_ERR_INVALID, "the column slice and K must be multiples of 8");
+  if (c_ranks == nullptr || a == nullptr || b_slice == nullptr)
+    return fail(HST_ERR_INVALID, "null pointer");
+  HST_TRY(check_problem(a, b_slice, c_ranks[rank], m, cols, k, n_total));
+  DeviceState* dev = nullptr;
+  HST_TRY(device_state(&dev));
+  const hst_gemm_config cfg{HST_FAMILY_PAIR, 256, block_n, block_k, 4, num_stages, group_m, 1};
+  const View va{static_cast<const __half*>(a), m, k, k, 1};
+  const View vb{static_cast<const __half*>(b_slice), k, cols, cols, 1};
+  Plan p;
+  HST_TRY(make_plan(&cfg, va, vb, m, cols, k, dev->sm_count, &p));
+  if (p.pack_a || p.pack_b) return fail(HST_ERR_INVALID, "operands must be 16-byte aligned row-major");
   if (m == 0) return HST_OK;
   PairFanoutArgs fanout = {};
   fanout.ldc = n_total;
   for (int q = 0; q < world; ++q) {
     if (q == rank) continue;
+    if (c_ranks[q] == nullptr) return fail(HST_ERR_INVALID, "null peer output");
     fanout.peers[fanout.count++] =
-        reinterpret_cast<uint64_t>(static_cast<__half*>(c_ranks[q]) + rank * l.cols);
+        reinterpret_cast<uint64_t>(static_cast<__half*>(c_ranks[q]) + rank * cols);
   }
-  return launch_column_pair(l, fanout, static_cast<cudaStream_t>(stream));
-}
-
-int hst_matmul_pair_band_copies(int32_t block_n, int32_t block_k, int32_t num_stages,
-                                int32_t group_m, const void* a, const void* b_slice,
-                                void* const* c_ranks, int32_t world, int32_t rank, int64_t m,
-                                int64_t n_total, int64_t k, uint32_t* band_flags, int64_t num_bands,
-                                uint32_t epoch, void* const* copy_streams, void* stream) {
-  ColumnLaunch l;
-  HST_TRY(prepare_column_launch(block_n, block_k, num_stages, group_m, a, b_slice, c_ranks, world,
-                                rank, m, n_total, k, &l));
-  if (m == 0) return HST_OK;
-  const int tiles_m = static_cast<int>(cdiv(m, 256));
-  const int tiles_n = static_cast<int>(cdiv(l.cols, l.plan.bn));
-  const int gm = l.plan.group_m;
-  const int bands = static_cast<int>(cdiv(tiles_m, gm));
-  if (num_bands != bands)
-    return fail(HST_ERR_INVALID, "%lld band words given, %d bands of %d tile rows needed",
-                static_cast<long long>(num_bands), bands, gm);
-  if (band_flags == nullptr || (reinterpret_cast<uintptr_t>(band_flags) & 3) != 0)
-    return fail(HST_ERR_INVALID, "band words must be non-null and 4-byte aligned");
-  if (epoch == 0) return fail(HST_ERR_INVALID, "epoch must be >= 1");
-  if (world > 1 && copy_streams == nullptr) return fail(HST_ERR_INVALID, "null copy streams");
-  for (int j = 0; j + 1 < world; ++j)
-    if (copy_streams[j] == nullptr) return fail(HST_ERR_INVALID, "null copy stream %d", j);
-  PfnStreamWaitValue32 wait_value = nullptr;
-  if (world > 1) HST_TRY(stream_wait_value_fn(&wait_value));
-  const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // The GEMM and the release kernel first: no copy stream's wait can then sit ahead of them in
-  // a hardware queue that the streams share.
-  PairFanoutArgs fanout = {};
-  fanout.ldc = n_total;
-  fanout.band_flags = band_flags;
-  HST_TRY(launch_column_pair(l, fanout, s));
-  band_release_kernel<<<static_cast<unsigned>(cdiv(bands, 128)), 128, 0, s>>>(band_flags, bands, tiles_m,
-                                                                               tiles_n, gm, epoch);
-  HST_CUDA(cudaGetLastError());
-  const size_t width = static_cast<size_t>(l.cols) * sizeof(__half);
-  const size_t pitch = static_cast<size_t>(n_total) * sizeof(__half);
-  for (int j = 0; j + 1 < world; ++j) {
-    const int q = (rank + 1 + j) % world;
-    const cudaStream_t cs = static_cast<cudaStream_t>(copy_streams[j]);
-    char* dst = reinterpret_cast<char*>(static_cast<__half*>(c_ranks[q]) + rank * l.cols);
-    const char* src = reinterpret_cast<const char*>(l.o.c);
-    for (int b = 0; b < bands; ++b) {
-      const int64_t row0 = static_cast<int64_t>(b) * gm * 256;
-      const int64_t rows = std::min<int64_t>(static_cast<int64_t>(gm) * 256, m - row0);
-      const CUresult r = wait_value(reinterpret_cast<CUstream>(cs), reinterpret_cast<CUdeviceptr>(band_flags + b),
-                                    band_target(epoch, b, tiles_m, tiles_n, gm), CU_STREAM_WAIT_VALUE_GEQ);
-      if (r != CUDA_SUCCESS) return fail(HST_ERR_CUDA, "cuStreamWaitValue32 failed (%d)", static_cast<int>(r));
-      HST_CUDA(cudaMemcpy2DAsync(dst + row0 * pitch, pitch, src + row0 * pitch, pitch, width,
-                                 static_cast<size_t>(rows), cudaMemcpyDeviceToDevice, cs));
-    }
-  }
-  return HST_OK;
+  Operands o;
+  o.m = static_cast<int>(m);
+  o.n = static_cast<int>(cols);
+  o.k = static_cast<int>(k);
+  o.a = va.ptr;
+  o.lda = k;
+  o.b = vb.ptr;
+  o.ldb = cols;
+  o.c = static_cast<__half*>(c_ranks[rank]) + rank * cols;
+  o.ldc = n_total;
+  if ((reinterpret_cast<uintptr_t>(o.c) & 15) != 0 || n_total % 8 != 0)
+    return fail(HST_ERR_INVALID, "output rows must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p.bn == 256 && p.bk == 64) return launch_pair<256, 64, false>(*dev, o, p.stages, p.group_m, 1, 0, s, &fanout);
+  if (p.bn == 128 && p.bk == 64) return launch_pair<128, 64, false>(*dev, o, p.stages, p.group_m, 1, 0, s, &fanout);
+  if (p.bn == 256 && p.bk == 128) return launch_pair<256, 128, false>(*dev, o, p.stages, p.group_m, 1, 0, s, &fanout);
+  if (p.bn == 128 && p.bk == 128) return launch_pair<128, 128, false>(*dev, o, p.stages, p.group_m, 1, 0, s, &fanout);
+  if (p.bn == 512 && p.bk == 64) return launch_pair<512, 64, false>(*dev, o, p.stages, p.group_m, 1, 0, s, &fanout);
+  return fail(HST_ERR_UNSUPPORTED, "no pair kernel for N %d, K %d", p.bn, p.bk);
 }
 
 int hst_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* y, int64_t ldy,

@@ -79,20 +79,14 @@ struct PairShape {
   }
 };
 
-// Column-parallel exchange of the persistent pair kernel, one of two forms:
-//   * fan-out: every finished 64-column sub-tile of this rank's C slice is also written, with
-//     coalesced 16-byte stores, into the same columns of the other ranks' C (peer pointers over
-//     NVLink). The local copy goes through the TMA store.
-//   * band counts: C goes to local memory only; when an epilogue warp's bulk stores of a whole
-//     tile have completed, it adds one to the word of the tile's row band (the tile rows of one
-//     raster group), so that 8 * tiles-in-band increments mark a band complete. The copy
-//     engines wait for those counts (stream memory waits) and copy each band to the peers.
+// Column-parallel fan-out of the persistent pair kernel: every finished 64-column sub-tile of
+// this rank's C slice is also written, with coalesced 16-byte stores, into the same columns of
+// the other ranks' C (peer pointers over NVLink). The local copy goes through the TMA store.
 constexpr int kMaxPeers = 8;
 struct PairFanoutArgs {
   uint64_t peers[kMaxPeers];  // other ranks' C base + this rank's column offset (elements)
   int count;                  // number of peers (0 = no fan-out)
   int64_t ldc;                // row stride of every rank's full C, elements
-  uint32_t* band_flags;       // band-count form: one word per band of group_m tile rows, or null
 };
 
 struct PairSplitArgs {
@@ -583,17 +577,6 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           acc_phase ^= 1u;
         }
       }
-      if (fanout.band_flags != nullptr && kb0 == 0) {
-        // Band counts: this warp's 32 rows of the tile are in C once its bulk stores are
-        // complete (the accumulator is already released, so the next tile's UMMAs run on).
-        if (lane == 0) {
-          bulk_wait_group<0>();
-          fence_proxy_async_global();
-          __threadfence_system();
-          atomicAdd(fanout.band_flags + pm / args.group_m, 1u);
-        }
-        __syncwarp();
-      }
     }
     if (lane == 0) bulk_wait_group<0>();
     if (fanout.count > 0) __threadfence_system();  // peer stores are visible before exit
@@ -714,24 +697,6 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     __syncwarp();
     tc_fence_after_sync();
     tmem_dealloc_pair(tmem_base, S::kTmemCols);
-  }
-}
-
-// The band-count word of a launch's band b after it: epoch * (8 increments per tile of the band),
-// modulo 2^32 (stream memory waits compare cyclically).
-__host__ __device__ inline uint32_t band_target(uint32_t epoch, int b, int tiles_m, int tiles_n, int group_m) {
-  const int rows = min(group_m, tiles_m - b * group_m);
-  return epoch * static_cast<uint32_t>(8 * rows * tiles_n);
-}
-
-// Runs after the band-count GEMM on its stream: sets every band word to this launch's target, so
-// that the copy streams' waits end even if the GEMM gave up early (its status word says so).
-__global__ void band_release_kernel(uint32_t* flags, int bands, int tiles_m, int tiles_n, int group_m,
-                                    uint32_t epoch) {
-  const int b = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x);
-  if (b < bands) {
-    *reinterpret_cast<volatile uint32_t*>(flags + b) = band_target(epoch, b, tiles_m, tiles_n, group_m);
-    __threadfence_system();
   }
 }
 

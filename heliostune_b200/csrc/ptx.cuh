@@ -167,12 +167,6 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// Orders this thread's completed bulk (async-proxy) writes to global memory before its later
-// generic-proxy accesses, e.g. the flag that publishes them.
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
 // L2 policies for TMA loads: streamed weights are evicted first, reused operands kept.
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;

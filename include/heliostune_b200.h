@@ -189,24 +189,6 @@ int hst_matmul_pair_fanout(int32_t block_n, int32_t block_k, int32_t num_stages,
                            const void* a, const void* b_slice, void* const* c_ranks, int32_t world,
                            int32_t rank, int64_t m, int64_t n_total, int64_t k, void* stream);
 
-/* The same column-parallel GEMM with the exchange on the copy engines (no reference
- * counterpart). The CTA-pair GEMM writes C_r into this rank's own C only and counts, in
- * band_flags[b] (num_bands = ceil(ceil(m / 256) / group_m) words of device memory, zero before
- * the first call, then left to these calls), the finished tiles of each band of group_m tile rows
- * (256 * group_m rows of C). copy_streams holds world - 1 streams; stream j waits (a stream
- * memory wait) for each band in turn and copies it, on the copy engines, into the same rows and
- * columns of peer (rank + 1 + j) % world's C. A small kernel after the GEMM on `stream` sets every
- * band word to its final value, so the waits end even if the GEMM fails. `epoch` is the number of
- * this call among the calls on these band words (1, 2, ...). Everything is enqueued in an order
- * that cannot deadlock (the GEMM before any wait). The caller makes `stream` wait for the copy
- * streams, then orders the ranks (a cross-rank barrier) before reading C; the copy streams must
- * start after the barrier that tells this rank the peers are done reading their C. */
-int hst_matmul_pair_band_copies(int32_t block_n, int32_t block_k, int32_t num_stages,
-                                int32_t group_m, const void* a, const void* b_slice,
-                                void* const* c_ranks, int32_t world, int32_t rank, int64_t m,
-                                int64_t n_total, int64_t k, uint32_t* band_flags, int64_t num_bands,
-                                uint32_t epoch, void* const* copy_streams, void* stream);
-
 /* Peer mappings for hst_matmul_pair_fanout (CUDA IPC; no multicast objects). hst_ipc_export
  * writes the 64-byte IPC handle of the allocation containing `ptr` and ptr's offset in it;
  * another process opens it with hst_ipc_import (the mapped base) and releases it with

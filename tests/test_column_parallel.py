@@ -3,7 +3,6 @@ ranks (CPU, host implementations of the GEMM and the assembly), plus the GPU ass
 
 from __future__ import annotations
 
-import dataclasses
 import os
 import socket
 
@@ -96,7 +95,7 @@ def test_assembly_kernel_and_single_rank_path() -> None:
     assert np.isfinite(c.float().cpu().numpy()).all()
 
 
-def _fused_rank(rank: int, world: int, port: int, queue, exchange: str) -> None:  # type: ignore[no-untyped-def]
+def _fused_rank(rank: int, world: int, port: int, queue) -> None:  # type: ignore[no-untyped-def]
     from datetime import timedelta
 
     from heliostune_b200.action_expansion import fp32_reference
@@ -117,20 +116,16 @@ def _fused_rank(rank: int, world: int, port: int, queue, exchange: str) -> None:
             (1000, 520, 2 * 1280, COLUMN_PARALLEL_WIDE),  # 256 x 512 tiles, ragged last tile
             (600, 1024, 2 * 3072, COLUMN_PARALLEL_CANDIDATE),
         )
-        # Copy-engine bands of 1 and 3 tile rows too: one band per tile row, a ragged last band.
-        band_rows = (None, 1, 3, 2)
-        for (m, k, n, candidate), rows in zip(cases, band_rows):
+        for m, k, n, candidate in cases:
             g = torch.Generator(device=device).manual_seed(m + k)
             a = (torch.randn((m, k), generator=g, device=device) / k**0.5).to(torch.float16)
             b = (torch.randn((k, n), generator=g, device=device) / k**0.5).to(torch.float16)
             shard = ColumnShard(n, world, rank)
-            fused = FusedColumnParallel(
-                m, n, device=device, candidate=candidate, exchange=exchange, band_rows=rows if exchange == "copies" else None
-            )
+            fused = FusedColumnParallel(m, n, device=device, candidate=candidate)
             expected = fp32_reference(a, b)
             gemm = None if candidate is None else (lambda x, y, c=candidate: launch(x, y, c))
             plain = column_parallel_matmul(a, shard.take(b), gemm=gemm)
-            for _ in range(3):  # later calls reuse the mapped outputs (and the band words)
+            for _ in range(2):  # the second call reuses the mapped outputs
                 c = fused(a, shard.take(b)).clone()
                 close = bool(torch.allclose(c.float(), expected, atol=1e-2, rtol=1e-2))
                 results.append(close and bool(torch.equal(c, plain)))
@@ -141,15 +136,14 @@ def _fused_rank(rank: int, world: int, port: int, queue, exchange: str) -> None:
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("exchange", ("stores", "copies"))
-def test_fused_column_parallel_on_two_gpus(exchange: str) -> None:
+def test_fused_column_parallel_on_two_gpus() -> None:
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     world = 2
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_fused_rank, args=(r, world, port, queue, exchange)) for r in range(world)]
+    procs = [ctx.Process(target=_fused_rank, args=(r, world, port, queue)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -158,22 +152,3 @@ def test_fused_column_parallel_on_two_gpus(exchange: str) -> None:
     results = [queue.get(timeout=10) for _ in range(world)]
     assert sorted(r for r, _ in results) == [0, 1]
     assert all(ok for _, ok in results)
-
-
-def test_copy_engine_bands_follow_the_raster_group() -> None:
-    from heliostune_b200.column_parallel import (
-        COLUMN_PARALLEL_CANDIDATE,
-        EXCHANGES,
-        band_tile_rows,
-        column_parallel_candidate,
-        exchange_candidate,
-    )
-
-    assert EXCHANGES == ("stores", "copies")
-    assert band_tile_rows(8) == 2 and band_tile_rows(4) == 4 and band_tile_rows(2) == 4
-    # The epilogue-store form keeps the slice GEMM's own raster; the copy-engine form changes
-    # only the raster group, which is the band.
-    assert exchange_candidate(8192, 7168, 8, "stores") == column_parallel_candidate(8192, 7168)
-    banded = exchange_candidate(8192, 7168, 8, "copies")
-    assert banded.config == dataclasses.replace(COLUMN_PARALLEL_CANDIDATE.config, group_m=2)
-    assert exchange_candidate(8192, 7168, 8, "copies", band_rows=5).config.group_m == 5

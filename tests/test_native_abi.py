@@ -110,23 +110,3 @@ def test_stream_k_planning_matches_the_python_rule(lib: ctypes.CDLL) -> None:
                 assert lib.hst_pair_stream_k_tiles(tiles, k_blocks, pairs, ctypes.byref(out)) == 0
                 assert out.value == pair_stream_k_tiles(tiles, k_blocks, pairs)
     assert lib.hst_pair_stream_k_tiles(4, 4, 0, ctypes.byref(out)) == _native.HST_ERR_INVALID
-
-
-def test_band_copy_entry_rejects_bad_launches_before_any_cuda_work(lib: ctypes.CDLL) -> None:
-    """hst_matmul_pair_band_copies validates the rank layout and pointers first, like the
-    epilogue fan-out entry it shares them with."""
-    outputs = (ctypes.c_void_p * 2)(None, None)
-    streams = (ctypes.c_void_p * 1)(None)
-    # block_n, block_k, stages, group_m, a, b, outputs, world, rank, m, n_total, k, band words,
-    # bands, epoch, copy streams, stream
-    args = [256, 64, 6, 2, 1, 1, outputs, 2, 0, 512, 1024, 512, 1, 1, 1, streams, None]
-    bad_world = list(args)
-    bad_world[7], bad_world[8] = 0, 0
-    assert lib.hst_matmul_pair_band_copies(*bad_world) == _native.HST_ERR_INVALID
-    uneven = list(args)
-    uneven[10] = 1025  # N does not split evenly over two ranks
-    assert lib.hst_matmul_pair_band_copies(*uneven) == _native.HST_ERR_INVALID
-    assert b"split evenly" in lib.hst_last_error()
-    assert lib.hst_matmul_pair_band_copies(*args) == _native.HST_ERR_INVALID  # null outputs
-    assert b"null" in lib.hst_last_error()
-
