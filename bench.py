@@ -84,7 +84,7 @@ def _config(args, workloads) -> dict[str, object]:
 
         (w,) = workloads
         exchange = (
-            "fused: GEMM epilogue stores every tile to all ranks over NVLink"
+            f"fused: GEMM epilogue writes every tile to all ranks over NVLink ({getattr(args, 'peer_writes', 'stores')})"
             if args.exchange == "fused" and world > 1
             else "NCCL all-gather + column assembly" if world > 1 else "none (one rank holds all of N)"
         )
@@ -668,7 +668,7 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
     if args.exchange == "fused" and world > 1:
         from heliostune_b200.column_parallel import FusedColumnParallel
 
-        fused = FusedColumnParallel(w.m, w.n, device=device)
+        fused = FusedColumnParallel(w.m, w.n, device=device, peer_writes=args.peer_writes)
 
         def step_on(x, y, events):
             return fused(x, y, phase_events=events)
@@ -1332,6 +1332,12 @@ def main() -> None:
         choices=("fused", "nccl"),
         default="fused",
         help="colpar: all-gather fused into the GEMM epilogue, or NCCL all-gather + assembly",
+    )
+    parser.add_argument(
+        "--peer-writes",
+        choices=("stores", "bulk"),
+        default="stores",
+        help="colpar fused exchange: epilogue 16-byte stores or TMA tensor stores into the peers' C",
     )
     args = parser.parse_args()
     if args.workload is None:

@@ -36,6 +36,9 @@ HST_ERR_WORKSPACE = 3
 HST_ERR_CUDA = 4
 HST_ERR_TIMEOUT = 5
 
+HST_PEER_STORES = 0
+HST_PEER_BULK = 1
+
 FAMILY_TILE = 0
 FAMILY_PERSISTENT = 1
 FAMILY_SPLIT_K = 2
@@ -170,7 +173,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "hst_ipc_import": ([_ptr, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
         "hst_ipc_close": ([_ptr], ctypes.c_int),
         "hst_matmul_pair_fanout": (
-            [_i32] * 4 + [_ptr, _ptr, ctypes.POINTER(ctypes.c_void_p), _i32, _i32, _i64, _i64, _i64, _ptr],
+            [_i32] * 4 + [_ptr, _ptr, ctypes.POINTER(ctypes.c_void_p), _i32, _i32, _i64, _i64, _i64, _i32, _ptr],
             ctypes.c_int,
         ),
         "hst_matmul_split_k_noalloc": (

@@ -95,14 +95,19 @@ def assemble_columns(gathered: torch.Tensor, out: torch.Tensor | None = None) ->
     return out
 
 
+#: How the fused GEMM writes into the peers' C: coalesced 16-byte stores from the epilogue warps,
+#: or one TMA tensor store per peer of every staged sub-tile.
+PEER_WRITES = {"stores": _native.HST_PEER_STORES, "bulk": _native.HST_PEER_BULK}
+
+
 class FusedColumnParallel:
     """Column-parallel GEMM whose all-gather is fused into the GEMM epilogue.
 
     Every rank allocates its full output ``C [M, N]`` once (``torch.empty``), exports its CUDA
     IPC handle, and maps every peer's output (``hst_ipc_*``). A call runs the persistent CTA-pair
     GEMM on this rank's column slice; each finished sub-tile goes to the local C by TMA and to
-    every peer's C by coalesced NVLink stores while the next tiles compute
-    (``hst_matmul_pair_fanout``). NCCL barriers before and after the launch order the ranks: no
+    every peer's C over NVLink while the next tiles compute (``hst_matmul_pair_fanout``), by
+    coalesced stores from the epilogue warps or by TMA tensor stores (``peer_writes``). NCCL barriers before and after the launch order the ranks: no
     peer writes into a C that is still being read, and C is complete when the call returns.
     The returned tensor is this object's buffer and is overwritten by the next call.
     """
@@ -115,9 +120,13 @@ class FusedColumnParallel:
         group: dist.ProcessGroup | None = None,
         candidate: ActionCandidate | None = None,
         device: torch.device | None = None,
+        peer_writes: str = "stores",
     ) -> None:
         import ctypes
 
+        if peer_writes not in PEER_WRITES:
+            raise ValueError(f"peer_writes must be one of {tuple(PEER_WRITES)}, not {peer_writes!r}")
+        self.peer_writes = peer_writes
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -185,6 +194,7 @@ class FusedColumnParallel:
                 m,
                 self.shard.n_total,
                 k,
+                PEER_WRITES[self.peer_writes],
                 _stream(self.device),
             )
         )

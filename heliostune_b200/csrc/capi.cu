@@ -1164,7 +1164,10 @@ int hst_matmul_pair(int32_t block_n, int32_t block_k, int32_t num_stages, int32_
 
 int hst_matmul_pair_fanout(int32_t block_n, int32_t block_k, int32_t num_stages, int32_t group_m,
                            const void* a, const void* b_slice, void* const* c_ranks, int32_t world,
-                           int32_t rank, int64_t m, int64_t n_total, int64_t k, void* stream) {
+                           int32_t rank, int64_t m, int64_t n_total, int64_t k, int32_t peer_writes,
+                           void* stream) {
+  if (peer_writes != HST_PEER_STORES && peer_writes != HST_PEER_BULK)
+    return fail(HST_ERR_INVALID, "peer_writes must be HST_PEER_STORES or HST_PEER_BULK");
   if (world < 1 || world > kMaxPeers + 1 || rank < 0 || rank >= world)
     return fail(HST_ERR_INVALID, "world %d / rank %d out of range (at most %d ranks)", world, rank,
                 kMaxPeers + 1);
@@ -1186,11 +1189,17 @@ int hst_matmul_pair_fanout(int32_t block_n, int32_t block_k, int32_t num_stages,
   if (m == 0) return HST_OK;
   PairFanoutArgs fanout = {};
   fanout.ldc = n_total;
-  for (int q = 0; q < world; ++q) {
-    if (q == rank) continue;
+  // Peers in the order rank + 1, rank + 2, ...: at any moment the ranks write to different peers.
+  for (int j = 1; j < world; ++j) {
+    const int q = (rank + j) % world;
     if (c_ranks[q] == nullptr) return fail(HST_ERR_INVALID, "null peer output");
-    fanout.peers[fanout.count++] =
-        reinterpret_cast<uint64_t>(static_cast<__half*>(c_ranks[q]) + rank * cols);
+    __half* slice = static_cast<__half*>(c_ranks[q]) + rank * cols;
+    if (peer_writes == HST_PEER_STORES) {
+      fanout.peers[fanout.count++] = reinterpret_cast<uint64_t>(slice);
+    } else {
+      if ((reinterpret_cast<uintptr_t>(slice) & 15) != 0) return fail(HST_ERR_INVALID, "peer output rows must be 16-byte aligned");
+      HST_TRY(encode_tiled_2d(&fanout.peer_maps[fanout.bulk_count++], slice, cols, m, n_total, 64, 32));
+    }
   }
   Operands o;
   o.m = static_cast<int>(m);

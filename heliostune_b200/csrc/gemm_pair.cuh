@@ -80,13 +80,20 @@ struct PairShape {
 };
 
 // Column-parallel fan-out of the persistent pair kernel: every finished 64-column sub-tile of
-// this rank's C slice is also written, with coalesced 16-byte stores, into the same columns of
-// the other ranks' C (peer pointers over NVLink). The local copy goes through the TMA store.
+// this rank's C slice is also written into the same columns of the other ranks' C over NVLink,
+// in one of two forms. The local copy goes through the TMA store.
+//   * stores (count > 0): the epilogue warp reads the staged sub-tile back once per lane and
+//     writes it to every peer with coalesced 16-byte stores (peer pointers);
+//   * bulk (bulk_count > 0): the warp's elected lane issues one more TMA tensor store of the
+//     staged sub-tile per peer (each peer's C slice as a tensor map), in the same bulk group as
+//     the local one, so the copy engine of the SM moves it while the warp drains on.
 constexpr int kMaxPeers = 8;
 struct PairFanoutArgs {
-  uint64_t peers[kMaxPeers];  // other ranks' C base + this rank's column offset (elements)
-  int count;                  // number of peers (0 = no fan-out)
-  int64_t ldc;                // row stride of every rank's full C, elements
+  CUtensorMap peer_maps[kMaxPeers];  // bulk form: peer q's C slice [m, cols], 64 x 32 boxes
+  uint64_t peers[kMaxPeers];         // stores form: peer C base + this rank's column offset
+  int count;                         // stores form: number of peers (0 = none)
+  int bulk_count;                    // bulk form: number of peer maps (0 = none)
+  int64_t ldc;                       // row stride of every rank's full C, elements
 };
 
 struct PairSplitArgs {
@@ -482,6 +489,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           __syncwarp();
           if (lane == 0) {
             tma_store_2d(&map_c, dst, n0 + c * 64, row0);
+            for (int q = 0; q < fanout.bulk_count; ++q) tma_store_2d(&fanout.peer_maps[q], dst, n0 + c * 64, row0);
             bulk_commit_group();
           }
           if (fanout.count > 0) {
@@ -579,7 +587,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       }
     }
     if (lane == 0) bulk_wait_group<0>();
-    if (fanout.count > 0) __threadfence_system();  // peer stores are visible before exit
+    if (fanout.count > 0 || fanout.bulk_count > 0) __threadfence_system();  // peer writes visible before exit
     __syncwarp();
   }
 

@@ -178,16 +178,23 @@ int hst_gated_mlp_stream(int32_t block_m, int32_t block_k, int32_t num_stages, i
                          const void* w_up, int64_t ld_up, void* out, int64_t ldo, int64_t m,
                          int64_t n, int64_t k, void* stream);
 
+/* Peer writes of hst_matmul_pair_fanout: coalesced 16-byte stores from the epilogue warps, or
+ * one TMA tensor store per peer of each staged sub-tile. */
+#define HST_PEER_STORES 0
+#define HST_PEER_BULK 1
+
 /* Fused column-parallel GEMM (no reference counterpart). Rank `rank` of `world` (<= 9) holds
  * A [m, k] and its column slice B_r [k, n_total / world], both row-major contiguous. c_ranks[q]
  * is rank q's full output C [m, n_total] (row-major, ldc = n_total) as mapped into this process
- * (e.g. symmetric memory); the CTA-pair GEMM writes C_r = A B_r into columns
+ * (e.g. CUDA IPC); the CTA-pair GEMM writes C_r = A B_r into columns
  * [rank * n_total / world, (rank + 1) * n_total / world) of its own C by TMA and of every peer's
- * C by coalesced peer stores as each tile finishes, so the exchange overlaps the GEMM. The
- * caller orders the ranks afterwards (a cross-rank barrier on the stream) before reading C. */
+ * C (peer_writes: HST_PEER_STORES or HST_PEER_BULK) as each tile finishes, so the exchange
+ * overlaps the GEMM. The caller orders the ranks afterwards (a cross-rank barrier on the stream)
+ * before reading C. */
 int hst_matmul_pair_fanout(int32_t block_n, int32_t block_k, int32_t num_stages, int32_t group_m,
                            const void* a, const void* b_slice, void* const* c_ranks, int32_t world,
-                           int32_t rank, int64_t m, int64_t n_total, int64_t k, void* stream);
+                           int32_t rank, int64_t m, int64_t n_total, int64_t k, int32_t peer_writes,
+                           void* stream);
 
 /* Peer mappings for hst_matmul_pair_fanout (CUDA IPC; no multicast objects). hst_ipc_export
  * writes the 64-byte IPC handle of the allocation containing `ptr` and ptr's offset in it;

@@ -95,7 +95,7 @@ def test_assembly_kernel_and_single_rank_path() -> None:
     assert np.isfinite(c.float().cpu().numpy()).all()
 
 
-def _fused_rank(rank: int, world: int, port: int, queue) -> None:  # type: ignore[no-untyped-def]
+def _fused_rank(rank: int, world: int, port: int, queue, peer_writes: str) -> None:  # type: ignore[no-untyped-def]
     from datetime import timedelta
 
     from heliostune_b200.action_expansion import fp32_reference
@@ -121,7 +121,7 @@ def _fused_rank(rank: int, world: int, port: int, queue) -> None:  # type: ignor
             a = (torch.randn((m, k), generator=g, device=device) / k**0.5).to(torch.float16)
             b = (torch.randn((k, n), generator=g, device=device) / k**0.5).to(torch.float16)
             shard = ColumnShard(n, world, rank)
-            fused = FusedColumnParallel(m, n, device=device, candidate=candidate)
+            fused = FusedColumnParallel(m, n, device=device, candidate=candidate, peer_writes=peer_writes)
             expected = fp32_reference(a, b)
             gemm = None if candidate is None else (lambda x, y, c=candidate: launch(x, y, c))
             plain = column_parallel_matmul(a, shard.take(b), gemm=gemm)
@@ -136,14 +136,15 @@ def _fused_rank(rank: int, world: int, port: int, queue) -> None:  # type: ignor
 
 
 @pytest.mark.gpu
-def test_fused_column_parallel_on_two_gpus() -> None:
+@pytest.mark.parametrize("peer_writes", ("stores", "bulk"))
+def test_fused_column_parallel_on_two_gpus(peer_writes: str) -> None:
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     world = 2
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_fused_rank, args=(r, world, port, queue)) for r in range(world)]
+    procs = [ctx.Process(target=_fused_rank, args=(r, world, port, queue, peer_writes)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:

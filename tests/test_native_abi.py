@@ -110,3 +110,11 @@ def test_stream_k_planning_matches_the_python_rule(lib: ctypes.CDLL) -> None:
                 assert lib.hst_pair_stream_k_tiles(tiles, k_blocks, pairs, ctypes.byref(out)) == 0
                 assert out.value == pair_stream_k_tiles(tiles, k_blocks, pairs)
     assert lib.hst_pair_stream_k_tiles(4, 4, 0, ctypes.byref(out)) == _native.HST_ERR_INVALID
+
+
+def test_fanout_entry_rejects_an_unknown_peer_write_form(lib: ctypes.CDLL) -> None:
+    outputs = (ctypes.c_void_p * 2)(None, None)
+    rc = lib.hst_matmul_pair_fanout(256, 64, 6, 8, 1, 1, outputs, 2, 0, 512, 1024, 512, 7, None)
+    assert rc == _native.HST_ERR_INVALID
+    assert b"peer_writes" in lib.hst_last_error()
+
