@@ -65,6 +65,7 @@ EXPORTED_SYMBOLS = (
     "hst_matmul_split_k_noalloc",
     "hst_column_assemble",
     "hst_matmul_pair_fanout",
+    "hst_peer_barrier",
     "hst_ipc_export",
     "hst_ipc_import",
     "hst_ipc_close",
@@ -176,6 +177,7 @@ def _declare(lib: ctypes.CDLL) -> None:
             [_i32] * 4 + [_ptr, _ptr, ctypes.POINTER(ctypes.c_void_p), _i32, _i32, _i64, _i64, _i64, _i32, _ptr],
             ctypes.c_int,
         ),
+        "hst_peer_barrier": ([ctypes.POINTER(ctypes.c_void_p), _i32, _i32, _i32, ctypes.c_uint64, _ptr], ctypes.c_int),
         "hst_matmul_split_k_noalloc": (
             [_i32] * 6 + [_ptr, _i64, _i64, _ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i64, _ptr],
             ctypes.c_int,

@@ -107,8 +107,11 @@ class FusedColumnParallel:
     IPC handle, and maps every peer's output (``hst_ipc_*``). A call runs the persistent CTA-pair
     GEMM on this rank's column slice; each finished sub-tile goes to the local C by TMA and to
     every peer's C over NVLink while the next tiles compute (``hst_matmul_pair_fanout``), by
-    coalesced stores from the epilogue warps or by TMA tensor stores (``peer_writes``). NCCL barriers before and after the launch order the ranks: no
-    peer writes into a C that is still being read, and C is complete when the call returns.
+    coalesced stores from the epilogue warps or by TMA tensor stores (``peer_writes``). Barriers
+    on the stream before and after the launch order the ranks without NCCL
+    (``hst_peer_barrier``: each rank stores the call's epoch into barrier words kept behind every
+    peer's C and waits for the peers' stores into its own): no peer writes into a C that is still
+    being read, and C is complete when the call returns.
     The returned tensor is this object's buffer and is overwritten by the next call.
     """
 
@@ -137,8 +140,16 @@ class FusedColumnParallel:
             raise ValueError("the fused column-parallel GEMM runs the CTA-pair kernel")
         self.candidate = candidate
         self.device = device or torch.device("cuda", torch.cuda.current_device())
-        self.out = torch.empty((m, n_total), dtype=torch.float16, device=self.device)
-        self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+        # One allocation per rank, so one IPC mapping per peer: C, then (256-byte aligned) the
+        # 2 x world barrier words of hst_peer_barrier, zero before the first barrier.
+        c_bytes = m * n_total * 2
+        words_offset = -(-c_bytes // 256) * 256
+        storage = torch.empty(words_offset + 2 * self.world * 8, dtype=torch.uint8, device=self.device)
+        self.out = storage[:c_bytes].view(torch.float16).view(m, n_total)
+        self._words = storage[words_offset:].view(torch.int64)
+        self._words.zero_()
+        self._epoch = 0
+        torch.cuda.synchronize(self.device)  # zero before any peer can write into it
         lib = _native.library()
         handle = (ctypes.c_char * 64)()
         offset = ctypes.c_uint64(0)
@@ -160,10 +171,17 @@ class FusedColumnParallel:
             self._bases.append(base.value)
             pointers.append(base.value + off)
         self._pointers = (ctypes.c_void_p * self.world)(*pointers)
+        self._word_pointers = (ctypes.c_void_p * self.world)(*(p + words_offset for p in pointers))
 
-    def _barrier(self) -> None:
+    def _barrier(self, slot: int) -> None:
+        """Every rank's stream reaches this point before work after it runs (hst_peer_barrier:
+        stores into the peers' barrier words over NVLink and a bounded wait on its own)."""
         if self.world > 1:
-            dist.all_reduce(self._flag, group=self.group)
+            _native.check(
+                _native.library().hst_peer_barrier(
+                    self._word_pointers, self.world, self.rank, slot, self._epoch, _stream(self.device)
+                )
+            )
 
     def __call__(
         self,
@@ -179,7 +197,8 @@ class FusedColumnParallel:
             raise ValueError("operands must be row-major contiguous")
         if phase_events:
             phase_events[0].record()
-        self._barrier()  # every rank is done reading the previous result
+        self._epoch += 1
+        self._barrier(0)  # every rank is done reading the previous result
         _native.check(
             _native.library().hst_matmul_pair_fanout(
                 config.block_n,
@@ -200,7 +219,7 @@ class FusedColumnParallel:
         )
         if phase_events:
             phase_events[1].record()
-        self._barrier()  # every rank's slices have landed everywhere
+        self._barrier(1)  # every rank's slices have landed everywhere
         if phase_events:
             phase_events[2].record()
         return self.out

@@ -248,6 +248,24 @@ __global__ void probe_timeout_kernel(int* status, uint64_t limit_ns) {
   }
 }
 
+// Cross-rank barrier of the fused column-parallel GEMM over CUDA-IPC mappings of every rank's
+// barrier words ([2 slots][world] u64 each). Thread q < world, q != rank, stores `epoch` into
+// slot `slot`, entry `rank`, of rank q's words (release, system scope), then waits for this
+// rank's own entry q of that slot to reach `epoch` (acquire). The stores that came before on this
+// stream -- the GEMM's peer writes, whose threads fenced at system scope before they exited --
+// are visible to a peer once it sees the word. A wait that runs out sets kStatusPeerTimeout.
+struct PeerWords {
+  unsigned long long* ranks[kMaxPeers + 1];  // rank q's barrier words as mapped here
+};
+
+__global__ void peer_barrier_kernel(const __grid_constant__ PeerWords words, int world, int rank, int slot,
+                                    unsigned long long epoch, int* status) {
+  const int q = static_cast<int>(threadIdx.x);
+  if (q >= world || q == rank) return;
+  st_release_sys_u64(words.ranks[q] + slot * world + rank, epoch);
+  if (!wait_at_least_sys_u64(words.ranks[rank] + slot * world + q, epoch)) atomicOr(status, kStatusPeerTimeout);
+}
+
 int grid_for(int64_t total, int sms) {
   const int64_t blocks = cdiv(total, 256);
   return static_cast<int>(blocks < int64_t(sms) * 8 ? (blocks > 0 ? blocks : 1) : int64_t(sms) * 8);
@@ -1397,6 +1415,27 @@ int hst_ipc_import(const void* handle, void** base_out) {
 int hst_ipc_close(void* base) {
   if (base == nullptr) return fail(HST_ERR_INVALID, "null pointer");
   HST_CUDA(cudaIpcCloseMemHandle(base));
+  return HST_OK;
+}
+
+int hst_peer_barrier(void* const* words_ranks, int32_t world, int32_t rank, int32_t slot, uint64_t epoch,
+                     void* stream) {
+  if (world < 1 || world > kMaxPeers + 1 || rank < 0 || rank >= world)
+    return fail(HST_ERR_INVALID, "world %d / rank %d out of range (at most %d ranks)", world, rank, kMaxPeers + 1);
+  if (slot != 0 && slot != 1) return fail(HST_ERR_INVALID, "slot must be 0 or 1");
+  if (epoch == 0) return fail(HST_ERR_INVALID, "epoch must be >= 1");
+  if (words_ranks == nullptr) return fail(HST_ERR_INVALID, "null pointer");
+  PeerWords words = {};
+  for (int q = 0; q < world; ++q) {
+    if (words_ranks[q] == nullptr || (reinterpret_cast<uintptr_t>(words_ranks[q]) & 7) != 0)
+      return fail(HST_ERR_INVALID, "barrier words of rank %d null or not 8-byte aligned", q);
+    words.ranks[q] = static_cast<unsigned long long*>(words_ranks[q]);
+  }
+  if (world == 1) return HST_OK;
+  DeviceState* dev = nullptr;
+  HST_TRY(device_state(&dev));
+  peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(words, world, rank, slot, epoch, dev->status);
+  HST_CUDA(cudaGetLastError());
   return HST_OK;
 }
 

@@ -21,6 +21,7 @@ enum StatusBits : int {
   kStatusDrainTimeout = 1 << 3,
   kStatusProbeTimeout = 1 << 4,
   kStatusBadLaunch = 1 << 5,
+  kStatusPeerTimeout = 1 << 6,
 };
 
 // Default bound of one wait: two seconds. Every kernel here finishes in milliseconds.
@@ -362,6 +363,32 @@ __device__ __forceinline__ bool wait_flag_u64(const unsigned long long* flag,
       __nanosleep(100);
     }
     if (abort != nullptr && *abort) return false;
+    if (global_timer_ns() - start > limit_ns) return false;
+  }
+}
+
+// System-scope forms, for words another GPU writes or reads over NVLink.
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Waits until *word >= value (words only grow). Gives up after `limit_ns`; returns false then.
+__device__ __forceinline__ bool wait_at_least_sys_u64(const unsigned long long* word, unsigned long long value,
+                                                      uint64_t limit_ns = kWaitLimitNs) {
+  if (ld_acquire_sys_u64(word) >= value) return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i) {
+      if (ld_acquire_sys_u64(word) >= value) return true;
+      __nanosleep(64);
+    }
     if (global_timer_ns() - start > limit_ns) return false;
   }
 }

@@ -210,9 +210,20 @@ int hst_ipc_close(void* base);
 int hst_column_assemble(const void* src, void* dst, int64_t parts, int64_t rows,
                         int64_t cols_per_part, int64_t ldd, void* stream);
 
+/* Cross-rank barrier on a stream, for hst_matmul_pair_fanout's callers (no reference
+ * counterpart). words_ranks[q] is rank q's array of 2 * world uint64 barrier words as mapped into
+ * this process (hst_ipc_* for the peers), all zero before the first call. One small kernel
+ * stores `epoch` into word slot * world + rank of every peer's array and waits until this rank's
+ * words slot * world + q have all reached it; `epoch` grows by one per barrier round and the
+ * ranks pass the same one. Work enqueued after it on the stream starts once every rank has
+ * reached the barrier, and sees what the ranks' earlier kernels wrote. A wait bounded at two
+ * seconds that runs out sets status bit 64. */
+int hst_peer_barrier(void* const* words_ranks, int32_t world, int32_t rank, int32_t slot, uint64_t epoch,
+                     void* stream);
+
 /* Status word of a device: bits set by kernels whose bounded waits ran out (1 producer,
- * 2 UMMA issuer, 4 epilogue, 8 drain, 16 timeout probe). Synchronises the device.
- * clear != 0 resets it afterwards. */
+ * 2 UMMA issuer, 4 epilogue, 8 drain, 16 timeout probe, 64 peer barrier). Synchronises the
+ * device. clear != 0 resets it afterwards. */
 int hst_status(int device, int* bits, int clear);
 
 /* Allocation-free split-K (no counterpart in the reference). For callers that cannot allocate
