@@ -177,7 +177,10 @@ def _declare(lib: ctypes.CDLL) -> None:
             [_i32] * 4 + [_ptr, _ptr, ctypes.POINTER(ctypes.c_void_p), _i32, _i32, _i64, _i64, _i64, _i32, _ptr],
             ctypes.c_int,
         ),
-        "hst_peer_barrier": ([ctypes.POINTER(ctypes.c_void_p), _i32, _i32, _i32, ctypes.c_uint64, _ptr], ctypes.c_int),
+        "hst_peer_barrier": (
+            [ctypes.POINTER(ctypes.c_void_p), _i32, _i32, _i32, ctypes.c_uint64, ctypes.c_uint64, _ptr],
+            ctypes.c_int,
+        ),
         "hst_matmul_split_k_noalloc": (
             [_i32] * 6 + [_ptr, _i64, _i64, _ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i64, _ptr],
             ctypes.c_int,

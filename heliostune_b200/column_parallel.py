@@ -179,7 +179,7 @@ class FusedColumnParallel:
         if self.world > 1:
             _native.check(
                 _native.library().hst_peer_barrier(
-                    self._word_pointers, self.world, self.rank, slot, self._epoch, _stream(self.device)
+                    self._word_pointers, self.world, self.rank, slot, self._epoch, 0, _stream(self.device)
                 )
             )
 

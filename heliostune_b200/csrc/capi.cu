@@ -259,11 +259,12 @@ struct PeerWords {
 };
 
 __global__ void peer_barrier_kernel(const __grid_constant__ PeerWords words, int world, int rank, int slot,
-                                    unsigned long long epoch, int* status) {
+                                    unsigned long long epoch, uint64_t limit_ns, int* status) {
   const int q = static_cast<int>(threadIdx.x);
   if (q >= world || q == rank) return;
   st_release_sys_u64(words.ranks[q] + slot * world + rank, epoch);
-  if (!wait_at_least_sys_u64(words.ranks[rank] + slot * world + q, epoch)) atomicOr(status, kStatusPeerTimeout);
+  if (!wait_at_least_sys_u64(words.ranks[rank] + slot * world + q, epoch, limit_ns))
+    atomicOr(status, kStatusPeerTimeout);
 }
 
 int grid_for(int64_t total, int sms) {
@@ -1419,7 +1420,9 @@ int hst_ipc_close(void* base) {
 }
 
 int hst_peer_barrier(void* const* words_ranks, int32_t world, int32_t rank, int32_t slot, uint64_t epoch,
-                     void* stream) {
+                     uint64_t limit_ns, void* stream) {
+  if (limit_ns == 0) limit_ns = 10000000000ull;
+  if (limit_ns > 60000000000ull) return fail(HST_ERR_INVALID, "barrier limit above one minute");
   if (world < 1 || world > kMaxPeers + 1 || rank < 0 || rank >= world)
     return fail(HST_ERR_INVALID, "world %d / rank %d out of range (at most %d ranks)", world, rank, kMaxPeers + 1);
   if (slot != 0 && slot != 1) return fail(HST_ERR_INVALID, "slot must be 0 or 1");
@@ -1434,7 +1437,8 @@ int hst_peer_barrier(void* const* words_ranks, int32_t world, int32_t rank, int3
   if (world == 1) return HST_OK;
   DeviceState* dev = nullptr;
   HST_TRY(device_state(&dev));
-  peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(words, world, rank, slot, epoch, dev->status);
+  peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(words, world, rank, slot, epoch, limit_ns,
+                                                                       dev->status);
   HST_CUDA(cudaGetLastError());
   return HST_OK;
 }

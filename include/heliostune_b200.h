@@ -216,10 +216,11 @@ int hst_column_assemble(const void* src, void* dst, int64_t parts, int64_t rows,
  * stores `epoch` into word slot * world + rank of every peer's array and waits until this rank's
  * words slot * world + q have all reached it; `epoch` grows by one per barrier round and the
  * ranks pass the same one. Work enqueued after it on the stream starts once every rank has
- * reached the barrier, and sees what the ranks' earlier kernels wrote. A wait bounded at two
- * seconds that runs out sets status bit 64. */
+ * reached the barrier, and sees what the ranks' earlier kernels wrote. The wait is bounded by
+ * limit_ns (0: ten seconds; at most one minute); when it runs out the kernel sets status bit 64
+ * and returns. */
 int hst_peer_barrier(void* const* words_ranks, int32_t world, int32_t rank, int32_t slot, uint64_t epoch,
-                     void* stream);
+                     uint64_t limit_ns, void* stream);
 
 /* Status word of a device: bits set by kernels whose bounded waits ran out (1 producer,
  * 2 UMMA issuer, 4 epilogue, 8 drain, 16 timeout probe, 64 peer barrier). Synchronises the

@@ -40,9 +40,9 @@ def test_invalid_arguments_become_value_errors() -> None:
 
 def test_peer_barrier_that_nobody_answers_times_out_and_reports() -> None:
     """hst_peer_barrier for rank 0 of two, the second "rank" a plain buffer on the same GPU that no
-    kernel ever writes back from: the bounded wait runs out (two seconds), sets status bit 64,
+    kernel ever writes back from: the bounded wait runs out, sets status bit 64,
     and the store into the other rank's words has landed. One GPU, one kernel; nothing waits on
-    another launch."""
+    another launch. The wait is bounded at 20 ms here."""
     import ctypes
 
     require_cuda()
@@ -52,7 +52,7 @@ def test_peer_barrier_that_nobody_answers_times_out_and_reports() -> None:
     mine = torch.zeros(4, dtype=torch.int64, device="cuda")
     other = torch.zeros(4, dtype=torch.int64, device="cuda")
     words = (ctypes.c_void_p * 2)(mine.data_ptr(), other.data_ptr())
-    _native.check(lib.hst_peer_barrier(words, 2, 0, 1, 5, torch.cuda.current_stream().cuda_stream))
+    _native.check(lib.hst_peer_barrier(words, 2, 0, 1, 5, 20_000_000, torch.cuda.current_stream().cuda_stream))
     bits = _native.status(device, clear=True)
     assert bits & 64, bits
     assert other.tolist() == [0, 0, 5, 0]  # slot 1, entry of rank 0

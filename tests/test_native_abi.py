@@ -121,15 +121,16 @@ def test_fanout_entry_rejects_an_unknown_peer_write_form(lib: ctypes.CDLL) -> No
 
 def test_peer_barrier_rejects_bad_arguments_before_any_cuda_work(lib: ctypes.CDLL) -> None:
     words = (ctypes.c_void_p * 2)(8, 16)
-    assert lib.hst_peer_barrier(words, 0, 0, 0, 1, None) == _native.HST_ERR_INVALID
-    assert lib.hst_peer_barrier(words, 2, 2, 0, 1, None) == _native.HST_ERR_INVALID
-    assert lib.hst_peer_barrier(words, 2, 0, 2, 1, None) == _native.HST_ERR_INVALID
+    assert lib.hst_peer_barrier(words, 0, 0, 0, 1, 0, None) == _native.HST_ERR_INVALID
+    assert lib.hst_peer_barrier(words, 2, 2, 0, 1, 0, None) == _native.HST_ERR_INVALID
+    assert lib.hst_peer_barrier(words, 2, 0, 2, 1, 0, None) == _native.HST_ERR_INVALID
     assert b"slot" in lib.hst_last_error()
-    assert lib.hst_peer_barrier(words, 2, 0, 1, 0, None) == _native.HST_ERR_INVALID
+    assert lib.hst_peer_barrier(words, 2, 0, 1, 0, 0, None) == _native.HST_ERR_INVALID
     assert b"epoch" in lib.hst_last_error()
     unaligned = (ctypes.c_void_p * 2)(8, 12)
-    assert lib.hst_peer_barrier(unaligned, 2, 0, 1, 1, None) == _native.HST_ERR_INVALID
+    assert lib.hst_peer_barrier(unaligned, 2, 0, 1, 1, 0, None) == _native.HST_ERR_INVALID
     assert b"aligned" in lib.hst_last_error()
+    assert lib.hst_peer_barrier(words, 2, 0, 1, 1, 61_000_000_000, None) == _native.HST_ERR_INVALID
     # One rank: nothing to wait for, nothing launched.
-    assert lib.hst_peer_barrier(words, 1, 0, 0, 1, None) == _native.HST_OK
+    assert lib.hst_peer_barrier(words, 1, 0, 0, 1, 0, None) == _native.HST_OK
 
