@@ -80,11 +80,11 @@ def _config(args, workloads) -> dict[str, object]:
     """The ``config`` object of the JSON line; both arms print the same one."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.workload == "colpar":
-        from heliostune_b200.column_parallel import column_parallel_candidate
+        from heliostune_b200.column_parallel import column_parallel_candidate, default_peer_writes
 
         (w,) = workloads
         exchange = (
-            f"fused: GEMM epilogue writes every tile to all ranks over NVLink ({getattr(args, 'peer_writes', 'stores')})"
+            f"fused: GEMM epilogue writes every tile to all ranks over NVLink ({getattr(args, 'peer_writes', None) or default_peer_writes(world)})"
             if args.exchange == "fused" and world > 1
             else "NCCL all-gather + column assembly" if world > 1 else "none (one rank holds all of N)"
         )
@@ -1336,8 +1336,11 @@ def main() -> None:
     parser.add_argument(
         "--peer-writes",
         choices=("stores", "bulk"),
-        default="stores",
-        help="colpar fused exchange: epilogue 16-byte stores or TMA tensor stores into the peers' C",
+        default=None,
+        help=(
+            "colpar fused exchange: epilogue 16-byte stores or TMA tensor stores into the peers' C "
+            "(default: bulk at 2 GPUs, else stores)"
+        ),
     )
     args = parser.parse_args()
     if args.workload is None:

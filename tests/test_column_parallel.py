@@ -153,3 +153,11 @@ def test_fused_column_parallel_on_two_gpus(peer_writes: str) -> None:
     results = [queue.get(timeout=10) for _ in range(world)]
     assert sorted(r for r, _ in results) == [0, 1]
     assert all(ok for _, ok in results)
+
+
+def test_default_peer_writes_by_rank_count() -> None:
+    from heliostune_b200.column_parallel import PEER_WRITES, default_peer_writes
+
+    assert set(PEER_WRITES) == {"stores", "bulk"}
+    assert default_peer_writes(2) == "bulk"
+    assert [default_peer_writes(n) for n in (1, 4, 8)] == ["stores"] * 3
