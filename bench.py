@@ -782,7 +782,8 @@ def run_colpar(args: argparse.Namespace) -> dict[str, object] | None:
                 "the whole job's; time from the first copy to the last, max over ranks"
             ),
         },
-        "gpu_launches": (1 if fused is not None or world == 1 else 2) * args.steps,
+        # Per step: barrier, fused GEMM, barrier; or the GEMM and the assembly; or the GEMM alone.
+        "gpu_launches": (3 if fused is not None else 1 if world == 1 else 2) * args.steps,
         "clocks": sampler.summary(epoch0, epoch1),
         "status_bits": _native.status(local_rank),
     }
