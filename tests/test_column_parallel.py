@@ -161,3 +161,63 @@ def test_default_peer_writes_by_rank_count() -> None:
     assert set(PEER_WRITES) == {"stores", "bulk"}
     assert default_peer_writes(2) == "bulk"
     assert [default_peer_writes(n) for n in (1, 4, 8)] == ["stores"] * 3
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("peer_writes", ("stores", "bulk"))
+@pytest.mark.parametrize(("m", "k", "n_total", "block_n"), ((1000, 1032, 2 * 1024, 256), (600, 520, 2 * 1280, 512)))
+def test_fanout_writes_on_one_gpu(peer_writes: str, m: int, k: int, n_total: int, block_n: int) -> None:
+    """hst_matmul_pair_fanout as rank 0 of two whose "peer" output is a second buffer on the same
+    GPU: one launch, no cross-kernel wait. Both outputs hold the same bits in rank 0's columns,
+    equal to the plain pair GEMM's and within the FP32 reference's tolerance; nothing else is
+    written."""
+    import ctypes
+
+    from heliostune_b200 import _native
+    from heliostune_b200.action_configs import ActionCandidate, PairConfig
+    from heliostune_b200.action_expansion import fp32_reference, launch
+    from heliostune_b200.column_parallel import PEER_WRITES
+
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA is unavailable")
+    g = torch.Generator(device="cuda").manual_seed(m + k)
+    a = (torch.randn((m, k), generator=g, device="cuda") / k**0.5).to(torch.float16)
+    cols = n_total // 2
+    b0 = (torch.randn((k, cols), generator=g, device="cuda") / k**0.5).to(torch.float16)
+    sentinel = torch.tensor(-7.0, dtype=torch.float16)
+    c0 = torch.full((m, n_total), sentinel.item(), dtype=torch.float16, device="cuda")
+    c1 = torch.full((m, n_total), sentinel.item(), dtype=torch.float16, device="cuda")
+    config = PairConfig(256, block_n, 64, 4, 4 if block_n == 512 else 6, 8)
+    outputs = (ctypes.c_void_p * 2)(c0.data_ptr(), c1.data_ptr())
+    _native.check(
+        _native.library().hst_matmul_pair_fanout(
+            config.block_n, config.block_k, config.num_stages, config.group_m, a.data_ptr(), b0.data_ptr(),
+            outputs, 2, 0, m, n_total, k, PEER_WRITES[peer_writes], torch.cuda.current_stream().cuda_stream,
+        )
+    )
+    plain = launch(a, b0, ActionCandidate(config))
+    torch.cuda.synchronize()
+    assert torch.equal(c0[:, :cols], plain) and torch.equal(c1[:, :cols], plain)
+    torch.testing.assert_close(plain.float(), fp32_reference(a, b0), atol=1e-2, rtol=1e-2)
+    assert bool((c0[:, cols:] == sentinel.item()).all()) and bool((c1[:, cols:] == sentinel.item()).all())
+    assert _native.status(torch.cuda.current_device()) == 0
+
+
+@pytest.mark.gpu
+def test_peer_barrier_passes_when_the_peer_has_arrived() -> None:
+    """hst_peer_barrier for rank 0 of two on one GPU with the peer's entry already stored: the
+    wait ends at once, the store into the other rank's words lands, no status bit is set."""
+    import ctypes
+
+    from heliostune_b200 import _native
+
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA is unavailable")
+    device = torch.cuda.current_device()
+    _native.status(device, clear=True)
+    mine = torch.tensor([0, 0, 0, 9], dtype=torch.int64, device="cuda")  # slot 1, entry of rank 1
+    other = torch.zeros(4, dtype=torch.int64, device="cuda")
+    words = (ctypes.c_void_p * 2)(mine.data_ptr(), other.data_ptr())
+    _native.check(_native.library().hst_peer_barrier(words, 2, 0, 1, 9, 0, torch.cuda.current_stream().cuda_stream))
+    assert other.tolist() == [0, 0, 9, 0]
+    assert _native.status(device) == 0
