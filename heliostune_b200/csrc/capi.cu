@@ -749,11 +749,16 @@ int launch_stream_cluster(const DeviceState& dev, const Operands& o, int stages,
   using S = ClusterStreamShape<NA, MP, BK>;
   static std::atomic<uint64_t> smem_done{0};
   HST_TRY(allow_smem(stream_cluster_kernel<NA, MP, BK, NORM>, smem_done));
-  // Exchange slots beside the ring when at least two stages still fit, else inside it.
+  // Exchange slots beside the ring when at least two stages still fit (asynchronous pushes), or
+  // when they cost no stage at all (plain remote stores: each CTA then pushes as soon as its own
+  // accumulator is complete instead of after the cluster's slowest main loop); else inside it.
   constexpr bool nrm = NORM;
   int early_stages = stages;
   while (early_stages > 2 && S::smem_bytes(early_stages, splits, true, nrm) > kMaxDynamicSmem) --early_stages;
-  const bool early = S::kAsyncPush && splits > 1 && S::smem_bytes(early_stages, splits, true, nrm) <= kMaxDynamicSmem;
+  int ring_stages = stages;
+  while (ring_stages > 2 && S::smem_bytes(ring_stages, splits, false, nrm) > kMaxDynamicSmem) --ring_stages;
+  const bool early = splits > 1 && S::smem_bytes(early_stages, splits, true, nrm) <= kMaxDynamicSmem &&
+                     (S::kAsyncPush || early_stages >= ring_stages);
   if (early) stages = early_stages;
   while (stages > 2 && S::smem_bytes(stages, splits, early, nrm) > kMaxDynamicSmem) --stages;
   if (S::smem_bytes(stages, splits, early, nrm) > kMaxDynamicSmem)

@@ -15,8 +15,10 @@
 //         when the slots fit beside the TMA ring ("early"; a cluster barrier armed at launch
 //         guarantees every receive barrier exists), else into the drained ring after a
 //         cluster barrier;
-//       - MP >= 128: plain remote stores into the drained ring between two cluster barriers
-//         (cheaper per byte than the asynchronous stores once each thread sends 128 words).
+//       - MP >= 128: plain remote stores (cheaper per byte than the asynchronous stores once
+//         each thread sends 128 words), into slots beside the ring pushed as soon as the CTA's
+//         own accumulator is complete when they cost no ring stage (completion by a cluster
+//         barrier), else into the drained ring between two cluster barriers.
 //     No workspace, no second kernel, no atomics; the result is bitwise reproducible.
 // With S = 1 the epilogue writes C straight from TMEM.
 //
