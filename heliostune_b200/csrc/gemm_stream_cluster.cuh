@@ -74,7 +74,6 @@ struct ClusterStreamShape {
   static constexpr uint32_t kIdesc = umma_idesc_f16(128, MP, true, false);
   static constexpr int kBarrierBytes = 256 + 16 * kStreamMaxStages;
   static constexpr bool kAsyncPush = MP <= 64;  // see the file comment
-  // Shared memory below the barriers: ring and exchange side by side, or overlaid.
   // Shared memory below the barriers: ring and exchange side by side, or overlaid; then the
   // per-stage gamma slices of the RMSNorm prologue.
   __host__ __device__ static constexpr int data_bytes(int stages, int splits, bool early, bool norm) {
